@@ -1,0 +1,450 @@
+"""Benchmark of the paged-KV hot path: one layer's KV append + paged decode.
+
+Workload ("config 2"): Qwen3-8B heads (32 q / 8 KV,
+head_dim 128), bf16, block_size 16, batch 256, every context 4096 tokens,
+65,536-block KV pool with seeded-permuted block tables; the append writes the
+256 new K/V rows, then decode attention reads 4 GiB of paged KV.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (launched by torchrun, one process per GPU) the KV heads are
+sharded N ways, as the engine's tensor parallelism does: rank r owns KV
+heads [r*8/N, (r+1)*8/N) and their q heads, its own cache shard and the same
+block tables. There is no collective on the data path; ranks meet only at the
+timing barriers. `value` = algorithmic bytes of all ranks / max rank time.
+
+`--impl reference` times the reference's CPU semantics (the oracle port, all
+host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+METRIC = "paged decode attn+KV-append HBM GB/s and tokens/s at 1/2/4/8 B200"
+TOTAL_Q_HEADS, TOTAL_KV_HEADS, HEAD_DIM, BLOCK_SIZE = 32, 8, 128, 16
+BATCH, CONTEXT = 256, 4096
+WORKLOAD = ("config2: Qwen3-8B decode step, one layer: KV append of 256 rows + paged GQA "
+            "decode, B 256, ctx 4096, Hq 32 / Hkv 8, D 128, bs 16, bf16")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--cpu-sample-seqs", type=int, default=16)
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="smaller batches are for profiler captures only")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.rows = []
+        self.proc = None
+        self.thread = None
+        self.window = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [c.strip() for c in line.split(",")]))
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        rows = [(t, r) for t, r in self.rows if len(r) >= 9 and r[0].isdigit()
+                and int(r[0]) in self.gpus]
+        in_window = rows
+        note = "during the timed region"
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [(t, r) for t, r in rows if t0 - 0.2 <= t <= t1 + 0.2]
+            if inside:
+                in_window = inside
+            else:
+                note = "around the timed region (shorter than the 200 ms sampling period)"
+        if not in_window:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for _, r in in_window if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for _, r in in_window if r[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({name for _, r in in_window for name, v in zip(names, r[5:9])
+                          if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(in_window), "when": note}
+
+
+# ---------------------------------------------------------------- workload --
+def make_shard(rank, world, device, batch=BATCH):
+    from my_vllm_b200 import workloads
+
+    if TOTAL_KV_HEADS % world:
+        raise SystemExit(f"--gpus must divide {TOTAL_KV_HEADS} (KV heads are sharded)")
+    return workloads.config2(device=device, seed=workloads.SEED_BASE + 2 + 1000 * rank,
+                             num_kv_heads=TOTAL_KV_HEADS // world,
+                             num_q_heads=TOTAL_Q_HEADS // world, batch=batch)
+
+
+def peaks():
+    try:
+        data = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu
+    summary (profiles/decode_config2_traffic.json), or None."""
+    path = REPO / "profiles" / "decode_config2_traffic.json"
+    try:
+        data = json.loads(path.read_text())
+        return int(data["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+# ------------------------------------------------------------ CPU baseline --
+def cpu_sample(num_seqs, seed=7):
+    """A bounded CPU-resident sample of config 2: `num_seqs` sequences of
+    4096 tokens with their own pages (same heads, dtype and layout)."""
+    from my_vllm_b200 import workloads
+
+    return workloads.config2(device="cpu", seed=seed, batch=num_seqs, ctx=CONTEXT)
+
+
+def time_oracle(w, threads):
+    """Run the oracle's append + attention over the sample on `threads`
+    host threads (sequences split across them); returns seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    sys.path.insert(0, str(REPO))
+    import oracle
+
+    def bits(t):
+        t = t.contiguous()
+        return t.view(torch.int16).numpy().view(np.uint16)
+
+    key, value = bits(w.key), bits(w.value)
+    k_cache, v_cache = bits(w.k_cache), bits(w.v_cache)
+    q = bits(w.q)
+    tables = w.block_tables.numpy()
+    lens = w.seq_lens.numpy()
+    slots = w.slot_mapping.numpy()
+    B = lens.size
+    chunks = [list(range(i, B, threads)) for i in range(min(threads, B))]
+
+    def run(ids):
+        idx = np.array(ids)
+        sub_tables = tables[idx]
+        indptr, pages = oracle.block_tables_to_csr(sub_tables, lens[idx], w.block_size)
+        return oracle.paged_attention(q[idx], k_cache, v_cache, indptr, pages, [1] * len(ids),
+                                      lens[idx].tolist(), dtype="bfloat16")
+
+    try:
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(limits=1)
+    except ImportError:  # pragma: no cover
+        limiter = None
+    t0 = time.perf_counter()
+    oracle.kv_append(key, value, k_cache, v_cache, slots)
+    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
+        list(pool.map(run, chunks))
+    dt = time.perf_counter() - t0
+    if limiter is not None:
+        limiter.unregister() if hasattr(limiter, "unregister") else None
+    return dt
+
+
+def cpu_baseline_leg(sample_seqs):
+    threads = os.cpu_count() or 1
+    w = cpu_sample(sample_seqs)
+    bytes_per_run = w.kv_bytes_read() + w.append_bytes()
+    time_oracle(w, threads)  # warm
+    runs, elapsed = 0, 0.0
+    while elapsed < 10.0 and runs < 20:
+        elapsed += time_oracle(w, threads)
+        runs += 1
+    gbs = bytes_per_run * runs / elapsed / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_seqs} of the 256 sequences (ctx 4096, 8 KV heads), append + "
+                      f"decode through the numpy oracle, {runs} runs in {elapsed:.1f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    w = cpu_sample(args.cpu_sample_seqs)
+    bytes_per_step = w.kv_bytes_read() + w.append_bytes()
+    for _ in range(args.warmup):
+        time_oracle(w, threads)
+    total = 0.0
+    for _ in range(args.steps):
+        total += time_oracle(w, threads)
+    gbs = bytes_per_step * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": CONTEXT,
+                   "parallelism": f"kv-head shards x{args.gpus}",
+                   "sample_per_step": f"{args.cpu_sample_seqs} sequences"},
+        "tokens_per_s": round(args.cpu_sample_seqs * args.steps / total, 2),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{args.cpu_sample_seqs} of 256 sequences per step"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours --
+def run_ours(args, rank, world, local_rank):
+    from my_vllm_b200 import B200PagedBackend, ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    w = make_shard(rank, world, device, args.batch)
+    backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, BLOCK_SIZE,
+                               torch.bfloat16)
+    common = w.common_metadata()
+    plan = backend.build_plan(common)
+    kv_bytes = w.kv_bytes_read()
+    app_bytes = w.append_bytes()
+    step_bytes = kv_bytes + app_bytes
+    n_parts = plan.metadata.decode_plan.num_parts
+    launches_per_step = 2 + (1 if n_parts > 1 else 0)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+        return backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = None
+    if rank == 0 and not args.no_clocks:
+        sampler = ClockSampler(range(world))
+        sampler.start()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+
+    # ---- device-timed region: K steps, per-launch events on the decode ----
+    dec_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    dec_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    wall0 = time.time()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+        dec_start[i].record(stream)
+        backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan)
+        dec_end[i].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(device)
+    wall1 = time.time()
+    barrier()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    decode_ms = sum(a.elapsed_time(b) for a, b in zip(dec_start, dec_end)) / args.steps
+    decode_ms_max = max_over_ranks(decode_ms)
+    backend.check_status()
+
+    # ---- end to end through the public API with host buffers ----
+    host = {name: getattr(w, name).cpu().pin_memory() for name in
+            ("q", "key", "value", "slot_mapping", "block_tables", "seq_lens",
+             "query_start_loc")}
+    dev = {name: torch.empty_like(getattr(w, name)) for name in host}
+    out_host = torch.empty(w.q.shape, dtype=w.q.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for name, t in host.items():
+            dev[name].copy_(t, non_blocking=True)
+        common_e2e = type(common)(**{**common.__dict__, "query_start_loc":
+                                     dev["query_start_loc"], "seq_lens": dev["seq_lens"],
+                                     "slot_mapping": dev["slot_mapping"],
+                                     "block_tables": dev["block_tables"]})
+        p = backend.build_plan(common_e2e)
+        ops.store_kvcache(dev["key"], dev["value"], w.k_cache, w.v_cache, dev["slot_mapping"])
+        out = backend.forward(dev["q"], dev["key"], dev["value"], w.k_cache, w.v_cache, p)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e2e_steps = max(1, min(args.steps, 100))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+
+    if sampler is not None:
+        sampler.mark(wall0, wall1)
+        sampler.stop()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_leg(args.cpu_sample_seqs)
+
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+
+    ms_per_step = elapsed_ms / args.steps
+    total_bytes = step_bytes * world
+    peak, peak_kind = peaks()
+    achieved = kv_bytes * world / (decode_ms_max * 1e-3) / 1e9  # all ranks' decode bytes
+    per_gpu_achieved = kv_bytes / (decode_ms * 1e-3) / 1e9
+    traffic = committed_traffic() if world == 1 else None
+    line = {
+        "metric": METRIC,
+        "value": round(total_bytes / (ms_per_step * 1e-3) / 1e9, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "global_batch": args.batch,
+            "seq_len": CONTEXT,
+            "parallelism": f"kv-head shards x{world} (tp{world}), no data-path collective",
+            "l2": "inputs larger than L2: 4 GiB of paged KV per step across the ranks",
+            "decode_split": n_parts,
+        },
+        "tokens_per_s": round(args.batch / (ms_per_step * 1e-3), 1),
+        "bytes_per_step": total_bytes,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "paged_decode_kernel",
+            "achieved": round(per_gpu_achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(per_gpu_achieved / peak, 4),
+            "peak_source": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+            "frac_of_8tbs_nominal": round(per_gpu_achieved / 8000.0, 4),
+            "algorithmic_bytes_per_launch": kv_bytes,
+            "launch_ms": round(decode_ms, 5),
+            "traffic": traffic,
+            "all_ranks_achieved": round(achieved, 1),
+        },
+        "e2e": {
+            "value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s",
+            "ms_per_step": round(e2e_ms, 5),
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "B200PagedBackend.build_plan/forward + ops.store_kvcache, pinned host buffers",
+        },
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if sampler is not None:
+        line["clocks"] = sampler.summary()
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world != args.gpus and "WORLD_SIZE" not in os.environ:
+        world = args.gpus
+    if world > 1 and "WORLD_SIZE" not in os.environ:
+        raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,173 @@
+/*
+ * b200_paged_attn.h — C ABI of the B200 (sm_100a) paged-KV attention path.
+ *
+ * The path has three kernels and a reduce pass:
+ *   1. KV append   — scatters new K/V rows into the paged cache by slot.
+ *   2. paged decode — one query token per sequence, GQA heads grouped per
+ *      KV head, TMA-staged 16-token tiles, split-KV with an LSE reduce.
+ *   3. paged prefill — chunked prefill over prefix-cached plus new tokens
+ *      with a bottom-right causal mask, tcgen05/TMEM tensor-core tiles.
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are device pointers; sizes and strides are in ELEMENTS unless
+ *     the name ends in _bytes.
+ *   - The paged cache is NHD: [num_blocks, block_size, num_kv_heads, head_dim]
+ *     (nanovllm/engine/model_runner.py:346), one tensor for K and one for V.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *     asynchronous on that stream; nothing here synchronises the device.
+ *   - `status` is an optional device int32 word. Kernels OR error bits into
+ *     it (B200_STATUS_*) instead of trapping; the host reads it when it
+ *     chooses to synchronise. Pass NULL to skip the reporting.
+ *   - Return value: B200_OK, or an error code with a message available from
+ *     b200_last_error() (thread-local).
+ */
+#ifndef B200_PAGED_ATTN_H_
+#define B200_PAGED_ATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT 1
+#define B200_ERR_UNSUPPORTED 2
+#define B200_ERR_CUDA 3
+
+/* device status bits (OR-ed into *status by the kernels) */
+#define B200_STATUS_SLOT_OUT_OF_RANGE 0x1
+#define B200_STATUS_PAGE_OUT_OF_RANGE 0x2
+#define B200_STATUS_WAIT_TIMEOUT 0x4
+#define B200_STATUS_TMEM_ALLOC_FAILED 0x8
+#define B200_STATUS_PLAN_EXCEEDED 0x10 /* a sequence is longer than the decode plan covers */
+
+/* element types of Q / K / V / O */
+#define B200_DTYPE_FLOAT16 0
+#define B200_DTYPE_BFLOAT16 1
+
+/* Version of this ABI (major * 100 + minor). */
+B200_API int b200_abi_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+B200_API const char* b200_last_error(void);
+
+/*
+ * KV append. Replaces the Triton `store_kvcache` launcher and kernel
+ * (nanovllm/layers/attention.py:11-41; CPU semantics in
+ * KVCacheStore.forward_native, attention.py:69-85).
+ *
+ * For every token i with slot_mapping[i] != -1, copies the row of
+ * `row_elems` (= num_kv_heads * head_dim) contiguous elements at
+ * key + i * key_row_stride to k_cache + slot * cache_slot_stride, and the
+ * value row likewise into v_cache. Slots of -1 are skipped. The copy is
+ * byte-exact for any element size. A slot outside [0, num_slots) is
+ * skipped and reported as B200_STATUS_SLOT_OUT_OF_RANGE.
+ *
+ *   slot_is_int64: 0 -> slot_mapping is int32 (the engine's layout,
+ *                  model_runner.py:451), 1 -> int64.
+ */
+B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
+                       const void* value, int64_t value_row_stride,
+                       void* k_cache, void* v_cache, int64_t cache_slot_stride,
+                       const void* slot_mapping, int32_t slot_is_int64,
+                       int64_t num_tokens, int64_t row_elems,
+                       int32_t elem_bytes, int64_t num_slots,
+                       int32_t* status, void* stream);
+
+/*
+ * Paged KV cache description (NHD). Strides are in elements; the innermost
+ * (head_dim) stride is 1. Every stride must be a multiple of 8 elements and
+ * both base pointers 16-byte aligned (TMA rules).
+ */
+typedef struct b200_paged_cache {
+  const void* k_cache;
+  const void* v_cache;
+  int64_t num_blocks;
+  int32_t block_size;   /* multiple of 16 */
+  int32_t num_kv_heads;
+  int32_t head_dim;     /* 128 */
+  int32_t dtype;        /* B200_DTYPE_* */
+  int64_t block_stride; /* elements between consecutive blocks */
+  int64_t slot_stride;  /* elements between consecutive slots of a block */
+  int64_t head_stride;  /* elements between consecutive KV heads */
+} b200_paged_cache;
+
+/*
+ * Decode work partition, computed once per scheduled batch (the engine calls
+ * build_plan once per step, model_runner.py:502) and reused by every layer.
+ *   num_parts       — KV partitions per (sequence, KV head); 1 = no split.
+ *   part_tokens     — tokens per partition (multiple of 16).
+ *   workspace_bytes — fp32 partial outputs + LSE the caller must provide
+ *                     to b200_paged_decode (0 when num_parts == 1).
+ */
+typedef struct b200_decode_plan {
+  int32_t num_parts;
+  int32_t part_tokens;
+  int64_t workspace_bytes;
+} b200_decode_plan;
+
+/*
+ * Plan the decode split for `num_seqs` sequences of at most `max_kv_len`
+ * tokens on the current device. `force_num_parts` > 0 pins the split count
+ * (tests); 0 lets the planner fill the SMs. Replaces the decode half of
+ * FlashInferBackend.build_plan (nanovllm/layers/attention_backend.py:827-839).
+ */
+B200_API int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim,
+                           int32_t block_size, int32_t max_kv_len,
+                           int32_t force_num_parts, b200_decode_plan* plan);
+
+/*
+ * Paged decode attention: one query token per sequence.
+ * q:   [num_seqs, num_q_heads, head_dim] with strides (q_seq_stride,
+ *      q_head_stride, 1); q head h reads KV head h / (num_q_heads/num_kv_heads).
+ * out: same shape, strides (out_seq_stride, out_head_stride, 1).
+ * block_tables: int32 [num_seqs, >= ceil(seq_len/block_size)] row stride
+ *      block_table_stride; seq_lens: int32 [num_seqs], each >= 1 and
+ *      including the token being decoded (model_runner.py:404-406).
+ * workspace: plan->workspace_bytes of device memory (may be NULL when 0).
+ * Replaces BatchDecodeWithPagedKVCacheWrapper.run as called from
+ * FlashInferBackend.forward (attention_backend.py:995-997, 1020-1025).
+ */
+B200_API int b200_paged_decode(const void* q, int64_t q_seq_stride, int64_t q_head_stride,
+                      const b200_paged_cache* cache,
+                      const int32_t* block_tables, int64_t block_table_stride,
+                      const int32_t* seq_lens, int32_t num_seqs,
+                      int32_t num_q_heads, void* out, int64_t out_seq_stride,
+                      int64_t out_head_stride, float softmax_scale,
+                      const b200_decode_plan* plan, void* workspace,
+                      int64_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Paged prefill / chunked-prefill attention over prefix-cached plus new
+ * tokens. Sequence s owns query rows [query_start_loc[s], query_start_loc[s+1])
+ * of q/out and seq_lens[s] KV tokens (the new ones included, already
+ * appended to the cache). Query row i of a q_len-row chunk attends to KV
+ * positions < seq_len - q_len + i + 1 (bottom-right causal mask,
+ * tests/test_attention_backend.py:686-693).
+ * max_q_len bounds the chunk length (host value from the metadata).
+ * Replaces BatchPrefillWithPagedKVCacheWrapper.run as called from
+ * FlashInferBackend.forward (attention_backend.py:992-994, 1014-1019).
+ */
+B200_API int b200_paged_prefill(const void* q, int64_t q_token_stride,
+                       int64_t q_head_stride, const b200_paged_cache* cache,
+                       const int32_t* block_tables, int64_t block_table_stride,
+                       const int32_t* seq_lens, const int32_t* query_start_loc,
+                       int32_t num_seqs, int32_t num_q_tokens, int32_t max_q_len,
+                       int32_t num_q_heads, void* out, int64_t out_token_stride,
+                       int64_t out_head_stride, float softmax_scale,
+                       int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* B200_PAGED_ATTN_H_ */

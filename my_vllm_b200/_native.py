@@ -1,0 +1,159 @@
+"""ctypes binding of the C ABI in ``include/b200_paged_attn.h``.
+
+This is the only module that touches the shared library. It loads the
+in-tree ``libb200_paged_attn.so`` and raises ``RuntimeError`` when the
+library is missing or a call fails: there is no fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libb200_paged_attn.so"
+
+B200_OK = 0
+B200_ERR_INVALID_ARGUMENT = 1
+B200_ERR_UNSUPPORTED = 2
+B200_ERR_CUDA = 3
+
+STATUS_SLOT_OUT_OF_RANGE = 0x1
+STATUS_PAGE_OUT_OF_RANGE = 0x2
+STATUS_WAIT_TIMEOUT = 0x4
+STATUS_TMEM_ALLOC_FAILED = 0x8
+STATUS_PLAN_EXCEEDED = 0x10
+
+DTYPE_FLOAT16 = 0
+DTYPE_BFLOAT16 = 1
+
+# Every symbol the header declares; tests check the library exports them all.
+EXPORTED_SYMBOLS = (
+    "b200_abi_version",
+    "b200_last_error",
+    "b200_store_kvcache",
+    "b200_paged_decode_plan",
+    "b200_paged_decode",
+    "b200_paged_prefill",
+)
+
+
+class PagedCache(ctypes.Structure):
+    """Mirror of ``b200_paged_cache``."""
+
+    _fields_ = [
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("block_stride", ctypes.c_int64),
+        ("slot_stride", ctypes.c_int64),
+        ("head_stride", ctypes.c_int64),
+    ]
+
+
+class DecodePlan(ctypes.Structure):
+    """Mirror of ``b200_decode_plan``."""
+
+    _fields_ = [
+        ("num_parts", ctypes.c_int32),
+        ("part_tokens", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+    def as_tuple(self) -> tuple[int, int, int]:
+        return (self.num_parts, self.part_tokens, self.workspace_bytes)
+
+
+_VP = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_F32 = ctypes.c_float
+
+_SIGNATURES = {
+    "b200_abi_version": ([], _I32),
+    "b200_last_error": ([], ctypes.c_char_p),
+    "b200_store_kvcache": (
+        [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _I32, _I64, _I64, _I32, _I64, _VP, _VP],
+        _I32,
+    ),
+    "b200_paged_decode_plan": (
+        [_I32, _I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(DecodePlan)],
+        _I32,
+    ),
+    "b200_paged_decode": (
+        [
+            _VP, _I64, _I64, ctypes.POINTER(PagedCache), _VP, _I64, _VP, _I32, _I32,
+            _VP, _I64, _I64, _F32, ctypes.POINTER(DecodePlan), _VP, _I64, _VP, _VP,
+        ],
+        _I32,
+    ),
+    "b200_paged_prefill": (
+        [
+            _VP, _I64, _I64, ctypes.POINTER(PagedCache), _VP, _I64, _VP, _VP, _I32,
+            _I32, _I32, _I32, _VP, _I64, _I64, _F32, _VP, _VP,
+        ],
+        _I32,
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Load the kernel library once; raise RuntimeError if it is unusable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIBRARY_PATH.exists():
+            raise RuntimeError(
+                f"B200 paged-attention library not built: {LIBRARY_PATH} is missing "
+                "(run `python -m my_vllm_b200.build`)"
+            )
+        lib = ctypes.CDLL(str(LIBRARY_PATH))
+        for name, (argtypes, restype) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+        return lib
+
+
+def library_available() -> bool:
+    try:
+        load_library()
+    except (RuntimeError, OSError):
+        return False
+    return True
+
+
+def check(rc: int, what: str) -> None:
+    """Turn a non-zero C-ABI return code into the reference's error types."""
+    if rc == B200_OK:
+        return
+    message = load_library().b200_last_error().decode(errors="replace")
+    text = f"{what}: {message}"
+    if rc == B200_ERR_INVALID_ARGUMENT:
+        raise ValueError(text)
+    raise RuntimeError(text)
+
+
+def describe_status(bits: int) -> str:
+    names = []
+    for bit, name in (
+        (STATUS_SLOT_OUT_OF_RANGE, "slot out of range"),
+        (STATUS_PAGE_OUT_OF_RANGE, "page index out of range"),
+        (STATUS_WAIT_TIMEOUT, "pipeline wait timed out"),
+        (STATUS_TMEM_ALLOC_FAILED, "tensor-memory allocation failed"),
+        (STATUS_PLAN_EXCEEDED, "sequence longer than the decode plan"),
+    ):
+        if bits & bit:
+            names.append(name)
+    return ", ".join(names) if names else "ok"

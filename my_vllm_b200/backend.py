@@ -1,0 +1,436 @@
+"""``B200PagedBackend``: the reference engine's attention backend contract,
+served by the sm_100a kernels of this package.
+
+Lifecycle (nanovllm/layers/attention_backend.py:174-275):
+  * ``build_metadata(common)`` keeps the engine's dense ``block_tables`` as-is
+    (no CSR conversion, unlike FlashInferBackend.build_metadata :666-767) and
+    makes no device reads when ``common.trusted``.
+  * ``build_plan(common)`` classifies the batch once (same rule as
+    ``_classify_batch`` :1484-1491), plans the decode split on the host and
+    returns the engine's ``AttentionPlan`` with route WARMUP, PREFILL, DECODE
+    or MIXED_SPLIT.
+  * ``forward(q, k, v, k_cache, v_cache, plan)`` writes every route into one
+    backend-owned output buffer that is reused across layers (:905-920);
+    MIXED_SPLIT writes rows [0, P) with the prefill kernel and rows [P, T)
+    with the decode kernel, without concatenation (:1011-1026).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from types import MappingProxyType
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+
+from . import _native, ops
+from .contract import (
+    AttentionBackend,
+    AttentionBackendRegistry,
+    AttentionPlan,
+    AttentionRoute,
+    BatchType,
+    CommonAttentionMetadata,
+)
+
+BACKEND_NAME = "b200"
+SUPPORTED_HEAD_DIM = 128
+MAX_GQA_GROUP = 16
+
+
+@dataclass(frozen=True)
+class B200PagedMetadata:
+    """Backend metadata: the engine's dense tables plus the decode split."""
+
+    query_start_loc: torch.Tensor
+    seq_lens: torch.Tensor
+    block_tables: torch.Tensor | None
+    decode_plan: ops.DecodePlan | None
+
+    @property
+    def is_cacheless(self) -> bool:
+        return self.block_tables is None
+
+
+def validate_common_metadata(common: CommonAttentionMetadata, *, require_cuda: bool) -> None:
+    """The engine's metadata contract (attention_backend.py:1384-1481).
+
+    Type and shape checks always run; value checks that need a device read run
+    only for untrusted metadata, so a trusted plan never synchronises.
+    """
+    if not isinstance(common, CommonAttentionMetadata):
+        raise TypeError("common must be CommonAttentionMetadata")
+    for name in ("num_prefill_seqs", "num_decode_seqs", "num_prefill_tokens",
+                 "num_decode_tokens", "max_q_len", "max_kv_len", "num_kv_blocks",
+                 "num_prefill_kv_blocks"):
+        value = getattr(common, name)
+        if isinstance(value, bool) or not isinstance(value, int):
+            raise TypeError(f"common.{name} must be an int")
+        if value < 0:
+            raise ValueError(f"common.{name} must be non-negative")
+    if common.num_seqs <= 0:
+        raise ValueError("attention metadata must contain at least one sequence")
+    if common.num_decode_tokens != common.num_decode_seqs:
+        raise ValueError("decode suffix must contain one query token per sequence")
+    if not isinstance(common.trusted, bool):
+        raise TypeError("common.trusted must be a bool")
+    for name in ("query_start_loc", "seq_lens", "slot_mapping"):
+        tensor = getattr(common, name)
+        if not isinstance(tensor, torch.Tensor):
+            raise TypeError(f"common.{name} must be a torch.Tensor")
+        if tensor.dtype != torch.int32:
+            raise TypeError(f"common.{name} must have dtype torch.int32")
+        if tensor.ndim != 1:
+            raise ValueError(f"common.{name} must be one-dimensional")
+        if require_cuda and tensor.device.type != "cuda":
+            raise ValueError(f"common.{name} must be on CUDA")
+    if common.query_start_loc.numel() != common.num_seqs + 1:
+        raise ValueError("query_start_loc length must equal number of sequences + 1")
+    if common.seq_lens.numel() != common.num_seqs:
+        raise ValueError("seq_lens length must equal number of sequences")
+    if common.slot_mapping.numel() != common.num_query_tokens:
+        raise ValueError("slot_mapping length must equal number of query tokens")
+    if not common.trusted:
+        if int(common.query_start_loc[0].item()) != 0:
+            raise ValueError("query_start_loc must start at zero")
+        if int(common.query_start_loc[-1].item()) != common.num_query_tokens:
+            raise ValueError("query_start_loc must end at num_query_tokens")
+        query_lengths = common.query_start_loc[1:] - common.query_start_loc[:-1]
+        if common.num_decode_seqs and not bool(
+            torch.all(query_lengths[common.num_prefill_seqs:] == 1).item()
+        ):
+            raise ValueError("every decode sequence must have one query token")
+        if not bool(torch.all(common.seq_lens > 0).item()):
+            raise ValueError("all KV sequence lengths must be positive")
+    block_tables = common.block_tables
+    if block_tables is not None:
+        if not isinstance(block_tables, torch.Tensor):
+            raise TypeError("common.block_tables must be a torch.Tensor")
+        if block_tables.dtype != torch.int32:
+            raise TypeError("common.block_tables must have dtype torch.int32")
+        if block_tables.ndim != 2:
+            raise ValueError("common.block_tables must be two-dimensional")
+        if block_tables.size(0) != common.num_seqs:
+            raise ValueError("block_tables row count must equal number of sequences")
+        if require_cuda and block_tables.device.type != "cuda":
+            raise ValueError("common.block_tables must be on CUDA")
+
+
+def classify_batch(common: CommonAttentionMetadata) -> BatchType:
+    """Single batch classification point (attention_backend.py:1484-1491)."""
+    if common.num_prefill_seqs == 0:
+        if common.num_decode_seqs <= 0:
+            raise ValueError("pure decode batch must contain decode requests")
+        return BatchType.PURE_DECODE
+    if common.num_decode_seqs == 0:
+        return BatchType.PURE_PREFILL
+    return BatchType.MIXED
+
+
+def cacheless_varlen_attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, common: CommonAttentionMetadata
+) -> torch.Tensor:
+    """Causal attention without a cache for the engine's memory-sizing warmup
+    (the WARMUP route; the engine's own helper is attention_backend.py:1556-1624).
+    Runs once at start-up on the GPU, outside the serving hot path."""
+    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
+        raise ValueError("cacheless attention expects rank-3 Q/K/V")
+    if k.shape != v.shape:
+        raise ValueError("cacheless key and value shapes must match")
+    if q.size(0) != k.size(0):
+        raise ValueError("cacheless warmup requires matching query and KV token counts")
+    if q.size(1) % k.size(1):
+        raise ValueError("query head count must be divisible by KV head count")
+    boundaries = common.query_start_loc.cpu().tolist()
+    repeat = q.size(1) // k.size(1)
+    scale = 1.0 / (q.size(-1) ** 0.5)
+    outputs = []
+    for start, end in zip(boundaries[:-1], boundaries[1:]):
+        qs = q[start:end].transpose(0, 1).unsqueeze(0)
+        ks = k[start:end].transpose(0, 1).unsqueeze(0)
+        vs = v[start:end].transpose(0, 1).unsqueeze(0)
+        if repeat != 1:
+            ks = ks.repeat_interleave(repeat, dim=1)
+            vs = vs.repeat_interleave(repeat, dim=1)
+        out = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=scale)
+        outputs.append(out.squeeze(0).transpose(0, 1))
+    return torch.cat(outputs, dim=0) if outputs else torch.empty_like(q)
+
+
+class B200PagedBackend(AttentionBackend):
+    """Paged KV attention on hand-written sm_100a kernels (TMA + tensor cores)."""
+
+    backend_name = BACKEND_NAME
+    supports_full_decode_graph = False
+
+    def __init__(
+        self,
+        num_q_heads: int,
+        num_kv_heads: int,
+        head_dim: int,
+        block_size: int,
+        dtype: torch.dtype,
+        *,
+        decode_num_parts: int = 0,
+    ) -> None:
+        super().__init__(num_q_heads, num_kv_heads, head_dim, block_size, dtype)
+        reason = _static_support_reason(
+            num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, head_dim=head_dim,
+            block_size=block_size, dtype=dtype,
+        )
+        if reason is not None:
+            if "dtype" in reason:
+                raise TypeError(reason)
+            raise ValueError(reason)
+        _native.load_library()  # RuntimeError when the kernels are not built
+        self.decode_num_parts = int(decode_num_parts)
+        self._planned_route: str | None = None
+        self._route_counts = {route.value: 0 for route in AttentionRoute}
+        self._output_buffer: torch.Tensor | None = None
+        self._workspace: torch.Tensor | None = None
+        self._status: torch.Tensor | None = None
+
+    # ------------------------------------------------------------ capability --
+    @classmethod
+    def support_reason(
+        cls,
+        *,
+        block_size: int,
+        dtype: torch.dtype,
+        device: torch.device | str | None = None,
+        num_q_heads: int | None = None,
+        num_kv_heads: int | None = None,
+        head_dim: int | None = None,
+        **_: Any,
+    ) -> str | None:
+        reason = _static_support_reason(
+            num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, head_dim=head_dim,
+            block_size=block_size, dtype=dtype,
+        )
+        if reason is not None:
+            return reason
+        if not torch.cuda.is_available():
+            return "a CUDA device is required"
+        selected = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device()
+        )
+        if selected.type != "cuda":
+            return "a CUDA device is required"
+        index = selected.index if selected.index is not None else torch.cuda.current_device()
+        major, minor = torch.cuda.get_device_capability(index)
+        if (major, minor) != (10, 0):
+            return f"kernels are built for sm_100a (B200); device is sm_{major}{minor}"
+        if not _native.library_available():
+            return f"kernel library {_native.LIBRARY_PATH.name} is not built"
+        return None
+
+    @property
+    def planned_route(self) -> str | None:
+        return self._planned_route
+
+    @property
+    def route_counts(self):
+        return MappingProxyType(dict(self._route_counts))
+
+    # ------------------------------------------------------------ status word --
+    def status_tensor(self, device: torch.device) -> torch.Tensor:
+        """Device word the kernels OR error bits into (never read implicitly)."""
+        if self._status is None or self._status.device != device:
+            self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._status
+
+    def check_status(self) -> None:
+        """Synchronising check of the device status word; raises on errors."""
+        if self._status is None:
+            return
+        bits = int(self._status.item())
+        if bits:
+            self._status.zero_()
+            raise RuntimeError(f"B200 attention kernels reported: {_native.describe_status(bits)}")
+
+    # -------------------------------------------------------------- metadata --
+    def build_metadata(self, common: CommonAttentionMetadata) -> B200PagedMetadata:
+        validate_common_metadata(common, require_cuda=True)
+        if common.block_tables is None:
+            return B200PagedMetadata(common.query_start_loc, common.seq_lens, None, None)
+        decode_plan = None
+        if common.num_decode_seqs:
+            decode_plan = ops.plan_decode(
+                common.num_decode_seqs, self.num_q_heads, self.num_kv_heads, self.head_dim,
+                self.block_size, self._decode_max_kv_len(common), self.decode_num_parts,
+            )
+        return B200PagedMetadata(
+            common.query_start_loc, common.seq_lens, common.block_tables, decode_plan
+        )
+
+    def _decode_max_kv_len(self, common: CommonAttentionMetadata) -> int:
+        """Upper bound of the decode sequences' KV length, from host values only."""
+        bound = common.max_kv_len
+        counts = common.block_counts
+        if isinstance(counts, tuple) and len(counts) == common.num_seqs and counts:
+            decode_counts = counts[common.num_prefill_seqs:]
+            if decode_counts:
+                bound = min(bound, max(decode_counts) * self.block_size) if bound else (
+                    max(decode_counts) * self.block_size
+                )
+        if bound <= 0:
+            # Untrusted metadata without host bounds: one read is the price.
+            bound = int(common.seq_lens[common.num_prefill_seqs:].max().item())
+        return bound
+
+    def build_plan(
+        self, common: CommonAttentionMetadata, metadata: B200PagedMetadata | None = None
+    ) -> AttentionPlan:
+        if metadata is None:
+            metadata = self.build_metadata(common)
+        if not isinstance(metadata, B200PagedMetadata):
+            raise TypeError("B200 backend requires B200PagedMetadata")
+        batch_type = classify_batch(common)
+        if metadata.is_cacheless:
+            route = AttentionRoute.WARMUP
+        elif batch_type is BatchType.PURE_PREFILL:
+            route = AttentionRoute.PREFILL
+        elif batch_type is BatchType.PURE_DECODE:
+            route = AttentionRoute.DECODE
+        else:
+            route = AttentionRoute.MIXED_SPLIT
+        if metadata.decode_plan is not None and metadata.decode_plan.workspace_bytes:
+            self._ensure_workspace(metadata.decode_plan.workspace_bytes, common.seq_lens.device)
+        plan = AttentionPlan(batch_type, route, common, metadata)
+        self._planned_route = route.value
+        self._route_counts[route.value] += 1
+        return plan
+
+    def _ensure_workspace(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        ws = self._workspace
+        if ws is None or ws.numel() < nbytes or ws.device != device:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            self._workspace = ws
+        return ws
+
+    def _get_reusable_attention_output(self, q: torch.Tensor) -> torch.Tensor:
+        buffer = self._output_buffer
+        if (
+            buffer is None
+            or buffer.size(0) < q.size(0)
+            or buffer.shape[1:] != q.shape[1:]
+            or buffer.device != q.device
+            or buffer.dtype != q.dtype
+        ):
+            buffer = torch.empty_like(q)
+            self._output_buffer = buffer
+        return buffer[: q.size(0)]
+
+    # --------------------------------------------------------------- forward --
+    def forward(
+        self,
+        q: torch.Tensor,
+        k: torch.Tensor,
+        v: torch.Tensor,
+        k_cache: torch.Tensor,
+        v_cache: torch.Tensor,
+        plan: AttentionPlan,
+    ) -> torch.Tensor:
+        if not isinstance(plan, AttentionPlan):
+            raise TypeError("attention forward requires AttentionPlan")
+        metadata = plan.metadata
+        if not isinstance(metadata, B200PagedMetadata):
+            raise TypeError(f"{self.backend_name} plan carries incompatible backend metadata")
+        has_k = isinstance(k_cache, torch.Tensor) and k_cache.numel() > 0
+        has_v = isinstance(v_cache, torch.Tensor) and v_cache.numel() > 0
+        if has_k != has_v:
+            raise ValueError("key and value caches must both be present or absent")
+        common = plan.common
+
+        if plan.route is AttentionRoute.WARMUP or not has_k:
+            if has_k:
+                raise ValueError("warmup route requires an empty KV cache")
+            out = cacheless_varlen_attention(q, k, v, common)
+            scratch = self._get_reusable_attention_output(q)
+            scratch.copy_(out)
+            return scratch
+
+        self._validate_inputs(q, k_cache, v_cache)
+        if metadata.is_cacheless:
+            raise ValueError("paged B200 attention requires page metadata")
+        if q.size(0) != common.num_query_tokens:
+            raise ValueError("query token count does not match the attention plan")
+        output = self._get_reusable_attention_output(q)
+        status = self.status_tensor(q.device)
+        block_tables = metadata.block_tables
+        assert block_tables is not None
+        nP = common.num_prefill_seqs
+        P = common.num_prefill_tokens
+
+        if plan.route is AttentionRoute.PREFILL:
+            expected = BatchType.PURE_PREFILL
+        elif plan.route is AttentionRoute.DECODE:
+            expected = BatchType.PURE_DECODE
+        elif plan.route is AttentionRoute.MIXED_SPLIT:
+            expected = BatchType.MIXED
+        else:
+            raise RuntimeError(f"invalid planned B200 route: {plan.route!r}")
+        if plan.batch_type is not expected:
+            raise ValueError("B200 route does not match the planned BatchType")
+
+        if nP:
+            ops.paged_prefill(
+                q[:P], k_cache, v_cache, block_tables[:nP], metadata.seq_lens[:nP],
+                metadata.query_start_loc[: nP + 1], output[:P], common.max_q_len,
+                self.softmax_scale, num_seqs=nP, status=status,
+            )
+        if common.num_decode_seqs:
+            assert metadata.decode_plan is not None
+            ops.paged_decode(
+                q[P:], k_cache, v_cache, block_tables[nP:], metadata.seq_lens[nP:],
+                output[P:], metadata.decode_plan, self.softmax_scale, self._workspace,
+                status=status,
+            )
+        return output
+
+    def _validate_inputs(self, q, k_cache, v_cache) -> None:
+        if q.device.type != "cuda" or q.dtype != self.dtype:
+            raise ValueError("query must be a CUDA tensor with the backend dtype")
+        if q.ndim != 3 or q.shape[1:] != (self.num_q_heads, self.head_dim):
+            raise ValueError("query must have shape [tokens, num_q_heads, head_dim]")
+        tail = (self.block_size, self.num_kv_heads, self.head_dim)
+        for name, cache in (("key", k_cache), ("value", v_cache)):
+            if cache.device != q.device or cache.dtype != self.dtype:
+                raise ValueError(f"{name} cache must share the query device and dtype")
+            if cache.ndim != 4 or cache.shape[1:] != tail:
+                raise ValueError(
+                    f"{name} cache must have shape [pages, block_size, num_kv_heads, head_dim]"
+                )
+
+
+def _static_support_reason(
+    *, num_q_heads, num_kv_heads, head_dim, block_size, dtype
+) -> str | None:
+    if dtype not in (torch.float16, torch.bfloat16):
+        return "dtype must be float16 or bfloat16"
+    if block_size is None or block_size <= 0 or block_size % 16:
+        return "block_size must be a positive multiple of 16"
+    if head_dim is not None and head_dim != SUPPORTED_HEAD_DIM:
+        return "head_dim must be 128"
+    if num_q_heads is not None and num_kv_heads is not None and num_kv_heads > 0:
+        if num_q_heads % num_kv_heads == 0 and num_q_heads // num_kv_heads > MAX_GQA_GROUP:
+            return f"at most {MAX_GQA_GROUP} query heads per KV head"
+    return None
+
+
+def register(registry=AttentionBackendRegistry, name: str = BACKEND_NAME) -> None:
+    """Register the backend with the engine's registry (idempotent)."""
+    if name in registry.registered_names():
+        if registry._BACKENDS.get(name) is B200PagedBackend:  # noqa: SLF001
+            return
+    registry.register(name, B200PagedBackend)
+
+
+__all__ = [
+    "B200PagedBackend",
+    "B200PagedMetadata",
+    "classify_batch",
+    "register",
+    "validate_common_metadata",
+]

@@ -1,0 +1,90 @@
+"""Build the sm_100a shared library that holds the paged-attention kernels.
+
+The library is built in-tree (``my_vllm_b200/libb200_paged_attn.so``) with a
+plain ``nvcc -shared`` so it travels with the source tree; there is no JIT
+cache. ``python -m my_vllm_b200.build`` rebuilds it when a source changed.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+CSRC_DIR = PACKAGE_DIR / "csrc"
+INCLUDE_DIR = PACKAGE_DIR.parent / "include"
+LIBRARY_NAME = "libb200_paged_attn.so"
+LIBRARY_PATH = PACKAGE_DIR / LIBRARY_NAME
+
+SOURCES = (
+    "kv_append.cu",
+    "paged_decode.cu",
+    "paged_prefill.cu",
+    "capi.cu",
+)
+
+NVCC_FLAGS = (
+    "-gencode",
+    "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "-O3",
+    "-std=c++17",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-fvisibility=hidden",
+    "-shared",
+)
+
+
+def _nvcc() -> str:
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    candidate = Path(cuda_home) / "bin" / "nvcc"
+    if candidate.exists():
+        return str(candidate)
+    found = shutil.which("nvcc")
+    if found is None:
+        raise RuntimeError("nvcc not found; set CUDA_HOME")
+    return found
+
+
+def _inputs() -> list[Path]:
+    files = [CSRC_DIR / name for name in SOURCES]
+    files += sorted(CSRC_DIR.glob("*.cuh"))
+    files += sorted(INCLUDE_DIR.glob("*.h"))
+    return files
+
+
+def is_stale() -> bool:
+    if not LIBRARY_PATH.exists():
+        return True
+    built = LIBRARY_PATH.stat().st_mtime
+    return any(path.stat().st_mtime > built for path in _inputs())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every kernel into one shared library; returns its path."""
+    if not force and not is_stale():
+        return LIBRARY_PATH
+    tmp = LIBRARY_PATH.with_suffix(".so.tmp")
+    cmd = [_nvcc(), *NVCC_FLAGS, "-o", str(tmp)]
+    if verbose:
+        cmd += ["-Xptxas", "-v"]
+    cmd += [str(CSRC_DIR / name) for name in SOURCES]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(
+            "nvcc failed:\n" + " ".join(cmd) + "\n" + result.stdout + result.stderr
+        )
+    if verbose:
+        sys.stderr.write(result.stderr)
+    os.replace(tmp, LIBRARY_PATH)
+    return LIBRARY_PATH
+
+
+if __name__ == "__main__":
+    path = build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(path)

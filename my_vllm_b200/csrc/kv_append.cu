@@ -1,0 +1,133 @@
+// kv_append.cu — KV-cache append: scatter new K/V rows into paged cache slots.
+//
+// Semantics follow nanovllm/layers/attention.py:11-41 (Triton
+// store_kvcache_kernel + launcher) and attention.py:69-85 (forward_native):
+// token i with slot s != -1 copies its K row to k_cache[s] and its V row to
+// v_cache[s]; slots of -1 (CUDA-graph padding) are skipped.
+//
+// Design: the work is pure HBM traffic (read one row, write one row), so the
+// kernel maps one 16-byte vector per thread, with consecutive threads on
+// consecutive vectors of the same row for coalesced 16-byte loads/stores.
+// A block covers whole rows of both K and V; the vector width falls back to
+// 8/4/2 bytes only when a pointer or stride is not 16-byte aligned.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace b200 {
+
+template <int kVec>
+struct VecType;
+template <>
+struct VecType<16> {
+  using type = uint4;
+};
+template <>
+struct VecType<8> {
+  using type = uint2;
+};
+template <>
+struct VecType<4> {
+  using type = uint32_t;
+};
+template <>
+struct VecType<2> {
+  using type = uint16_t;
+};
+
+template <int kVec, typename SlotT>
+__global__ void __launch_bounds__(256)
+    kv_append_kernel(const char* __restrict__ key, int64_t key_row_bytes_stride,
+                     const char* __restrict__ value,
+                     int64_t value_row_bytes_stride, char* __restrict__ k_cache,
+                     char* __restrict__ v_cache, int64_t cache_slot_bytes_stride,
+                     const SlotT* __restrict__ slot_mapping, int64_t num_tokens,
+                     int64_t vecs_per_row, int64_t num_slots,
+                     int32_t* status) {
+  using V = typename VecType<kVec>::type;
+  // Work item = (token, tensor in {K, V}, vector within row).
+  const int64_t per_token = 2 * vecs_per_row;
+  const int64_t total = num_tokens * per_token;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t token = idx / per_token;
+    const int64_t rem = idx - token * per_token;
+    const int is_v = rem >= vecs_per_row;
+    const int64_t vec = rem - (is_v ? vecs_per_row : 0);
+    const int64_t slot = static_cast<int64_t>(slot_mapping[token]);
+    if (slot == -1) continue;
+    if (slot < 0 || slot >= num_slots) {
+      if (vec == 0 && !is_v) report_status(status, B200_STATUS_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const char* src = (is_v ? value : key) +
+                      token * (is_v ? value_row_bytes_stride : key_row_bytes_stride) +
+                      vec * kVec;
+    char* dst = (is_v ? v_cache : k_cache) + slot * cache_slot_bytes_stride + vec * kVec;
+    *reinterpret_cast<V*>(dst) = __ldg(reinterpret_cast<const V*>(src));
+  }
+}
+
+template <int kVec>
+static cudaError_t launch_vec(const void* key, int64_t key_stride_b,
+                              const void* value, int64_t value_stride_b,
+                              void* k_cache, void* v_cache, int64_t slot_stride_b,
+                              const void* slots, bool slot64, int64_t num_tokens,
+                              int64_t row_bytes, int64_t num_slots,
+                              int32_t* status, cudaStream_t stream) {
+  const int64_t vecs = row_bytes / kVec;
+  const int64_t total = num_tokens * 2 * vecs;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  // Enough blocks to cover every SM several times over; the grid-stride loop
+  // handles the rest.
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  if (slot64) {
+    kv_append_kernel<kVec, int64_t><<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const char*>(key), key_stride_b,
+        static_cast<const char*>(value), value_stride_b,
+        static_cast<char*>(k_cache), static_cast<char*>(v_cache), slot_stride_b,
+        static_cast<const int64_t*>(slots), num_tokens, vecs, num_slots, status);
+  } else {
+    kv_append_kernel<kVec, int32_t><<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const char*>(key), key_stride_b,
+        static_cast<const char*>(value), value_stride_b,
+        static_cast<char*>(k_cache), static_cast<char*>(v_cache), slot_stride_b,
+        static_cast<const int32_t*>(slots), num_tokens, vecs, num_slots, status);
+  }
+  return cudaGetLastError();
+}
+
+// Picks the widest vector every pointer, stride and the row length allow.
+cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
+                             const void* value, int64_t value_row_stride,
+                             void* k_cache, void* v_cache,
+                             int64_t cache_slot_stride, const void* slot_mapping,
+                             bool slot64, int64_t num_tokens, int64_t row_elems,
+                             int32_t elem_bytes, int64_t num_slots,
+                             int32_t* status, cudaStream_t stream) {
+  const int64_t row_bytes = row_elems * elem_bytes;
+  const int64_t ks = key_row_stride * elem_bytes;
+  const int64_t vs = value_row_stride * elem_bytes;
+  const int64_t cs = cache_slot_stride * elem_bytes;
+  uint64_t align_bits = reinterpret_cast<uintptr_t>(key) |
+                        reinterpret_cast<uintptr_t>(value) |
+                        reinterpret_cast<uintptr_t>(k_cache) |
+                        reinterpret_cast<uintptr_t>(v_cache) |
+                        static_cast<uint64_t>(ks) | static_cast<uint64_t>(vs) |
+                        static_cast<uint64_t>(cs) | static_cast<uint64_t>(row_bytes);
+  if ((align_bits & 15) == 0)
+    return launch_vec<16>(key, ks, value, vs, k_cache, v_cache, cs, slot_mapping,
+                          slot64, num_tokens, row_bytes, num_slots, status, stream);
+  if ((align_bits & 7) == 0)
+    return launch_vec<8>(key, ks, value, vs, k_cache, v_cache, cs, slot_mapping,
+                         slot64, num_tokens, row_bytes, num_slots, status, stream);
+  if ((align_bits & 3) == 0)
+    return launch_vec<4>(key, ks, value, vs, k_cache, v_cache, cs, slot_mapping,
+                         slot64, num_tokens, row_bytes, num_slots, status, stream);
+  return launch_vec<2>(key, ks, value, vs, k_cache, v_cache, cs, slot_mapping,
+                       slot64, num_tokens, row_bytes, num_slots, status, stream);
+}
+
+}  // namespace b200

@@ -1,0 +1,60 @@
+// paged_decode.cuh — parameters and tile geometry of the decode kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+constexpr int kHeadDim = 128;       // Qwen3 head_dim; the kernels are built for it
+constexpr int kTileTokens = 16;     // KV tokens per tile (one MMA k-step of PV)
+constexpr int kHalfTileBytes = kTileTokens * 128;  // 16 rows x 64 elements x 2 B
+constexpr int kDecodeWarps = 4;
+constexpr int kDecodeStages = 3;
+constexpr int kDecodeStageBytes = 4 * kHalfTileBytes;  // K lo/hi + V lo/hi = 8 KiB
+constexpr int kDecodeStageArenaBytes = kDecodeWarps * kDecodeStages * kDecodeStageBytes;
+// Longest KV partition one CTA takes; the planner splits longer contexts.
+constexpr int kMaxPartTokens = 8192;
+constexpr int kMaxPartPages = kMaxPartTokens / kTileTokens + 8;
+constexpr int kMergeStride = kHeadDim + 4;  // padded fp32 row in the merge area
+constexpr int kDecodeSmemBytes = 1024 /* alignment slack */ + kDecodeStageArenaBytes +
+                                 kDecodeWarps * kDecodeStages * 8 + kMaxPartPages * 4;
+static_assert(kDecodeWarps * (32 + 16 * kMergeStride) * 4 <= kDecodeStageArenaBytes,
+              "merge area must fit in the stage arena");
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_seq_stride;
+  int64_t q_head_stride;
+  const int32_t* block_tables;
+  int64_t block_table_stride;
+  const int32_t* seq_lens;
+  void* out;
+  int64_t out_seq_stride;
+  int64_t out_head_stride;
+  float* part_o;    // [num_seqs, num_q_heads, num_parts, head_dim]
+  float* part_lse;  // [num_seqs, num_q_heads, num_parts], log2 domain
+  int num_parts;
+  int part_tokens;
+  int block_size;
+  int group;  // q heads per KV head
+  int num_q_heads;
+  int64_t num_blocks;
+  float scale_log2;  // softmax_scale * log2(e)
+  int32_t* status;
+};
+
+cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
+                                const DecodeParams& p, int dtype, int num_kv_heads,
+                                int num_seqs, cudaStream_t stream);
+int decode_ctas_per_sm();
+
+cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
+                             const void* value, int64_t value_row_stride,
+                             void* k_cache, void* v_cache, int64_t cache_slot_stride,
+                             const void* slot_mapping, bool slot64, int64_t num_tokens,
+                             int64_t row_elems, int32_t elem_bytes, int64_t num_slots,
+                             int32_t* status, cudaStream_t stream);
+
+}  // namespace b200

@@ -1,0 +1,225 @@
+"""Torch-tensor front ends of the three kernels.
+
+Each function checks its tensors the way the reference checks them before
+its own kernels run, then calls the C ABI on the current CUDA stream. There
+is no CPU path: a CPU tensor or a missing library raises.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+
+_DTYPES = {torch.float16: _native.DTYPE_FLOAT16, torch.bfloat16: _native.DTYPE_BFLOAT16}
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (the B200 path has no CPU fallback)")
+
+
+def store_kvcache(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    *,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Scatter K/V rows into cache slots; slots of -1 are skipped.
+
+    Drop-in for ``store_kvcache`` (nanovllm/layers/attention.py:34-41): same
+    arguments, the same stride assertions (attention.py:37-40), in place, on
+    the current stream. ``status`` (int32 CUDA tensor) collects
+    out-of-range-slot reports.
+    """
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    if not (key.stride(-1) == 1 and value.stride(-1) == 1):
+        raise AssertionError("key/value must be contiguous in head_dim")
+    if not (key.stride(1) == head_dim and value.stride(1) == head_dim):
+        raise AssertionError("key/value heads must be packed (stride(1) == head_dim)")
+    if not (k_cache.stride(1) == D and v_cache.stride(1) == D):
+        raise AssertionError("cache slots must be packed (stride(1) == num_kv_heads*head_dim)")
+    if slot_mapping.numel() != N:
+        raise AssertionError("slot_mapping must contain one slot per token")
+    for name, t in (("key", key), ("value", value), ("k_cache", k_cache),
+                    ("v_cache", v_cache), ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t)
+    if key.dtype != k_cache.dtype or value.dtype != v_cache.dtype or key.dtype != value.dtype:
+        raise ValueError("key, value and caches must share one dtype")
+    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("key and value caches must have the same shape and strides")
+    if k_cache.dim() >= 2 and k_cache.stride(0) != k_cache.size(1) * D:
+        raise ValueError("cache blocks must be contiguous ([num_blocks, block_size, ...])")
+    if value.shape != key.shape:
+        raise ValueError("key and value must have the same shape")
+    if slot_mapping.dtype not in (torch.int32, torch.int64):
+        raise TypeError("slot_mapping must be int32 or int64")
+    if slot_mapping.dim() != 1 or (N > 1 and slot_mapping.stride(0) != 1):
+        raise ValueError("slot_mapping must be a contiguous 1-D tensor")
+    if N == 0:
+        return
+    num_slots = k_cache.size(0) * k_cache.size(1) if k_cache.dim() >= 2 else k_cache.numel() // D
+    lib = _native.load_library()
+    rc = lib.b200_store_kvcache(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+        k_cache.data_ptr(), v_cache.data_ptr(), D,
+        slot_mapping.data_ptr(), 1 if slot_mapping.dtype == torch.int64 else 0,
+        N, D, key.element_size(), num_slots,
+        _ptr(status), _stream_handle(key.device),
+    )
+    _native.check(rc, "b200_store_kvcache")
+
+
+def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.PagedCache:
+    """Describe a pair of NHD caches ``[num_blocks, block_size, Hkv, D]``."""
+    if k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
+        raise ValueError(
+            "key and value caches must have shape [pages, block_size, num_kv_heads, head_dim]"
+        )
+    if k_cache.stride() != v_cache.stride():
+        raise ValueError("key and value caches must have identical strides")
+    if k_cache.dtype not in _DTYPES or v_cache.dtype != k_cache.dtype:
+        raise TypeError("caches must be float16 or bfloat16")
+    if k_cache.stride(3) != 1:
+        raise ValueError("cache head_dim must be contiguous")
+    return _native.PagedCache(
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0), k_cache.size(1),
+        k_cache.size(2), k_cache.size(3), _DTYPES[k_cache.dtype],
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+    )
+
+
+@dataclass(frozen=True)
+class DecodePlan:
+    """Host-side decode partition (``b200_decode_plan``), built once per step."""
+
+    num_parts: int
+    part_tokens: int
+    workspace_bytes: int
+
+    def as_native(self) -> _native.DecodePlan:
+        return _native.DecodePlan(self.num_parts, self.part_tokens, self.workspace_bytes)
+
+
+def plan_decode(
+    num_seqs: int,
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    block_size: int,
+    max_kv_len: int,
+    force_num_parts: int = 0,
+) -> DecodePlan:
+    """Choose the split-KV partition for a decode batch (host only, no sync)."""
+    plan = _native.DecodePlan()
+    rc = _native.load_library().b200_paged_decode_plan(
+        num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max(1, max_kv_len),
+        force_num_parts, plan,
+    )
+    _native.check(rc, "b200_paged_decode_plan")
+    return DecodePlan(*plan.as_tuple())
+
+
+def paged_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    out: torch.Tensor,
+    plan: DecodePlan,
+    softmax_scale: float,
+    workspace: torch.Tensor | None = None,
+    *,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode attention for ``q [B, Hq, D]`` into ``out [B, Hq, D]`` (in place)."""
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("block_tables", block_tables), ("seq_lens", seq_lens), ("out", out)):
+        _require_cuda(name, t)
+    if q.dim() != 3 or out.shape != q.shape or q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("q and out must be [tokens, num_q_heads, head_dim], head_dim contiguous")
+    if q.dtype != k_cache.dtype or out.dtype != q.dtype:
+        raise ValueError("query, output and caches must share one dtype")
+    if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("block_tables and seq_lens must be int32")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1 or seq_lens.stride(0) != 1:
+        raise ValueError("block_tables rows and seq_lens must be contiguous")
+    B = q.size(0)
+    if block_tables.size(0) < B or seq_lens.numel() < B:
+        raise ValueError("block_tables / seq_lens must have one row per sequence")
+    cache = paged_cache_desc(k_cache, v_cache)
+    ws_ptr, ws_bytes = None, 0
+    if plan.workspace_bytes:
+        if workspace is None or workspace.numel() * workspace.element_size() < plan.workspace_bytes:
+            raise ValueError("decode workspace smaller than the plan requires")
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    native_plan = plan.as_native()
+    rc = _native.load_library().b200_paged_decode(
+        q.data_ptr(), q.stride(0), q.stride(1), cache,
+        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(), B,
+        q.size(1), out.data_ptr(), out.stride(0), out.stride(1), float(softmax_scale),
+        native_plan, ws_ptr, ws_bytes, _ptr(status), _stream_handle(q.device),
+    )
+    _native.check(rc, "b200_paged_decode")
+    return out
+
+
+def paged_prefill(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    out: torch.Tensor,
+    max_q_len: int,
+    softmax_scale: float,
+    *,
+    num_seqs: int | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal paged prefill over ``num_seqs`` sequences into ``out`` (in place)."""
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("block_tables", block_tables), ("seq_lens", seq_lens),
+                    ("query_start_loc", query_start_loc), ("out", out)):
+        _require_cuda(name, t)
+    if q.dim() != 3 or out.shape != q.shape or q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("q and out must be [tokens, num_q_heads, head_dim], head_dim contiguous")
+    if q.dtype != k_cache.dtype or out.dtype != q.dtype:
+        raise ValueError("query, output and caches must share one dtype")
+    for name, t in (("block_tables", block_tables), ("seq_lens", seq_lens),
+                    ("query_start_loc", query_start_loc)):
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    S = seq_lens.numel() if num_seqs is None else num_seqs
+    if query_start_loc.numel() < S + 1 or block_tables.size(0) < S:
+        raise ValueError("query_start_loc / block_tables too short for num_seqs")
+    cache = paged_cache_desc(k_cache, v_cache)
+    rc = _native.load_library().b200_paged_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), cache,
+        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(),
+        query_start_loc.data_ptr(), S, q.size(0), int(max_q_len), q.size(1),
+        out.data_ptr(), out.stride(0), out.stride(1), float(softmax_scale),
+        _ptr(status), _stream_handle(q.device),
+    )
+    _native.check(rc, "b200_paged_prefill")
+    return out

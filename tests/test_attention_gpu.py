@@ -1,0 +1,225 @@
+"""Paged attention on the GPU through the engine-facing backend: parity with
+the reference (golden fixtures) and the oracle on all five configurations,
+plus size-independent properties at full size."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import from_storage, golden_module, load_golden
+from my_vllm_b200 import B200PagedBackend, ops, workloads
+from my_vllm_b200.contract import AttentionRoute, BatchType, CommonAttentionMetadata
+from parity import MAX_ABS, assert_close_to_oracle, sample_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _backend(w, **kw):
+    return B200PagedBackend(w.num_q_heads, w.num_kv_heads, w.head_dim, w.block_size,
+                            w.q.dtype, **kw)
+
+
+def _common(x, num_prefill, device):
+    qsl = x["query_start_loc"].tolist()
+    lens = x["seq_lens"].tolist()
+    bs = x["block_size"]
+    counts = tuple((n + bs - 1) // bs for n in lens)
+    q_lens = [qsl[i + 1] - qsl[i] for i in range(len(lens))]
+    return CommonAttentionMetadata(
+        num_prefill_seqs=num_prefill,
+        num_decode_seqs=len(lens) - num_prefill,
+        num_prefill_tokens=qsl[num_prefill],
+        num_decode_tokens=qsl[-1] - qsl[num_prefill],
+        query_start_loc=x["query_start_loc"].to(device),
+        seq_lens=x["seq_lens"].to(device),
+        slot_mapping=torch.arange(qsl[-1], dtype=torch.int32, device=device),
+        block_tables=x["block_tables"].to(device),
+        max_q_len=max(q_lens), max_kv_len=max(lens), block_counts=counts,
+        num_kv_blocks=sum(counts), num_prefill_kv_blocks=sum(counts[:num_prefill]),
+        trusted=True,
+    )
+
+
+@pytest.mark.parametrize("name", ["prefill", "decode", "mixed", "mixed3", "prefix_chunk",
+                                  "fp16_gqa4", "gqa8"])
+def test_golden_cases_match_reference(cuda_device, name):
+    mg = golden_module()
+    ql, kl, seed, n_prefill, kw = mg.ATTENTION_CASES[name]
+    x = mg.attention_inputs(ql, kl, seed, **kw)
+    g = load_golden(f"attn_{name}")
+    q = x["q"].to(cuda_device)
+    kc, vc = x["k_cache"].to(cuda_device), x["v_cache"].to(cuda_device)
+    backend = B200PagedBackend(q.size(1), kc.size(2), q.size(2), x["block_size"], q.dtype)
+    common = _common(x, n_prefill, cuda_device)
+    plan = backend.build_plan(common)
+    expected_route = {0: AttentionRoute.DECODE, len(ql): AttentionRoute.PREFILL}.get(
+        n_prefill, AttentionRoute.MIXED_SPLIT)
+    assert plan.route is expected_route
+    unused = q.new_empty((0, kc.size(2), q.size(2)))
+    out = backend.forward(q, unused, unused, kc, vc, plan)
+    torch.cuda.synchronize()
+    backend.check_status()
+    assert out.shape == q.shape and out.dtype == q.dtype
+    ref = from_storage(g["out"].view(np.uint16), q.dtype).to(cuda_device)
+    # the reference test's own check (test_attention_backend.py:416-418)
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=2e-2)
+    assert_close_to_oracle(out, g["out_f32"], q.dtype)
+
+
+def test_config1_append_then_decode_matches_reference(cuda_device):
+    mg = golden_module()
+    g = load_golden("config1")
+    w = mg.config1_inputs()
+    dev = cuda_device
+    kc, vc = w.k_cache.to(dev), w.v_cache.to(dev)
+    ops.store_kvcache(w.key.to(dev), w.value.to(dev), kc, vc, w.slot_mapping.to(dev))
+    backend = _backend(w)
+    x = dict(query_start_loc=w.query_start_loc, seq_lens=w.seq_lens,
+             block_tables=w.block_tables, block_size=w.block_size)
+    plan = backend.build_plan(_common(x, 0, dev))
+    assert plan.route is AttentionRoute.DECODE and plan.batch_type is BatchType.PURE_DECODE
+    q = w.q.to(dev)
+    out = backend.forward(q, q[:, :8], q[:, :8], kc, vc, plan)
+    torch.cuda.synchronize()
+    ref = from_storage(g["out"].view(np.uint16), q.dtype).to(dev)
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=2e-2)
+    assert_close_to_oracle(out, g["out_f32"], q.dtype)
+
+
+def _append_and_run(w, backend, dev):
+    ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+    common = w.common_metadata()
+    plan = backend.build_plan(common)
+    out = backend.forward(w.q, w.key[: w.num_tokens], w.value[: w.num_tokens], w.k_cache,
+                          w.v_cache, plan).clone()
+    torch.cuda.synchronize()
+    backend.check_status()
+    return out, plan
+
+
+def test_config2_decode_full_size(cuda_device):
+    w = workloads.config2(device=cuda_device)
+    backend = _backend(w)
+    out, plan = _append_and_run(w, backend, cuda_device)
+    assert plan.route is AttentionRoute.DECODE
+    expected, rows = sample_oracle(w, [0, 1, 77, 128, 200, 255])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+    # Paging property at full size: the same logical cache laid out over a
+    # different permutation of physical blocks gives bit-identical output.
+    perm = torch.randperm(w.k_cache.size(0), device=cuda_device,
+                          generator=torch.Generator(device=cuda_device).manual_seed(5))
+    inverse = torch.empty_like(perm)
+    inverse[perm] = torch.arange(perm.numel(), device=cuda_device)
+    k2 = torch.empty_like(w.k_cache)
+    v2 = torch.empty_like(w.v_cache)
+    k2[inverse] = w.k_cache
+    v2[inverse] = w.v_cache
+    w.k_cache, w.v_cache = k2, v2
+    w.block_tables = inverse[w.block_tables.long()].to(torch.int32)
+    common = w.common_metadata()
+    plan2 = backend.build_plan(common)
+    out2 = backend.forward(w.q, w.key, w.value, k2, v2, plan2)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+
+
+def test_config2_padded_batch_rows(cuda_device):
+    """264 appended rows, 8 of them CUDA-graph padding (slot -1): attention
+    over the 256 real rows is unchanged by the padding."""
+    w = workloads.config2(device=cuda_device, padded=True, batch=64, ctx=1024)
+    backend = _backend(w)
+    out, _ = _append_and_run(w, backend, cuda_device)
+    expected, rows = sample_oracle(w, [0, 31, 63])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+@pytest.mark.parametrize("parts", [1, 3, 7])
+def test_split_kv_partitions_agree(cuda_device, parts):
+    w = workloads.config2(device=cuda_device, batch=16, ctx=3000, pool_blocks=4096)
+    backend = _backend(w, decode_num_parts=parts)
+    out, plan = _append_and_run(w, backend, cuda_device)
+    assert plan.metadata.decode_plan.num_parts == parts
+    expected, rows = sample_oracle(w, list(range(16)))
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+def test_config3_mixed_chunked_prefill(cuda_device):
+    w = workloads.config3(device=cuda_device)
+    backend = _backend(w)
+    out, plan = _append_and_run(w, backend, cuda_device)
+    assert plan.route is AttentionRoute.MIXED_SPLIT and plan.batch_type is BatchType.MIXED
+    # every prefill row (4 x 512 tokens over shared prefixes) and a decode sample
+    expected, rows = sample_oracle(w, [0, 1, 2, 3])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    expected, rows = sample_oracle(w, [4, 50, 127])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+def test_config4_tensor_parallel_shard(cuda_device):
+    """One rank's shard of Qwen3-32B heads at tp 8 (8 q heads on 1 KV head)."""
+    w = workloads.config4(device=cuda_device, tp=8, batch=128)
+    backend = _backend(w)
+    out, _ = _append_and_run(w, backend, cuda_device)
+    expected, rows = sample_oracle(w, [0, 64, 127])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+@pytest.mark.parametrize("block_size", [16, 256])
+def test_config5_long_context_split_kv(cuda_device, block_size):
+    w = workloads.config5(device=cuda_device, block_size=block_size)
+    backend = _backend(w)
+    out, plan = _append_and_run(w, backend, cuda_device)
+    assert plan.metadata.decode_plan.num_parts > 1
+    expected, rows = sample_oracle(w, [0, 31])
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+def test_fp16_decode_tolerance(cuda_device):
+    w = workloads.config2(device=cuda_device, batch=8, ctx=777, pool_blocks=512,
+                          dtype=torch.float16)
+    backend = _backend(w)
+    out, _ = _append_and_run(w, backend, cuda_device)
+    expected, rows = sample_oracle(w, list(range(8)))
+    err = assert_close_to_oracle(out[rows], expected, torch.float16)
+    assert err <= MAX_ABS[torch.float16]
+
+
+def test_deterministic_repeat(cuda_device):
+    w = workloads.config3(device=cuda_device, num_decode=16)
+    backend = _backend(w)
+    out1, plan = _append_and_run(w, backend, cuda_device)
+    out2 = backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(out1.view(torch.int16), out2.view(torch.int16))
+
+
+def test_warmup_route_without_cache(cuda_device):
+    mg = golden_module()
+    torch.manual_seed(223)
+    q = torch.randn(4, 16, 128, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(4, 4, 128, device=cuda_device, dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    common = CommonAttentionMetadata(
+        num_prefill_seqs=2, num_decode_seqs=0, num_prefill_tokens=4, num_decode_tokens=0,
+        query_start_loc=torch.tensor([0, 3, 4], dtype=torch.int32, device=cuda_device),
+        seq_lens=torch.tensor([3, 1], dtype=torch.int32, device=cuda_device),
+        slot_mapping=torch.full((4,), -1, dtype=torch.int32, device=cuda_device),
+        block_tables=None, max_q_len=3, max_kv_len=3, trusted=True,
+    )
+    backend = B200PagedBackend(16, 4, 128, 16, torch.bfloat16)
+    plan = backend.build_plan(common)
+    assert plan.route is AttentionRoute.WARMUP
+    empty = torch.empty(0, device=cuda_device)
+    out = backend.forward(q, k, v, empty, empty, plan)
+    del mg
+    import oracle
+    from conftest import storage
+    # cacheless warmup == paged attention over a cache holding exactly k/v
+    kc = np.zeros((2, 16, 4, 128), np.uint16)
+    vc = np.zeros((2, 16, 4, 128), np.uint16)
+    kc[0, :3], vc[0, :3] = storage(k[:3]), storage(v[:3])
+    kc[1, :1], vc[1, :1] = storage(k[3:]), storage(v[3:])
+    ref = oracle.paged_attention_from_tables(storage(q), kc, vc, [[0], [1]], [3, 1], [0, 3, 4],
+                                             16, out_dtype="float32")
+    assert_close_to_oracle(out, ref, torch.bfloat16)

@@ -1,0 +1,111 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol the header
+declares, and rejects malformed arguments before touching the device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from my_vllm_b200 import _native, ops
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "b200_paged_attn.h"
+
+
+def _declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"B200_API\s+[\w\s\*]+?\b(b200_\w+)\s*\(", text)))
+
+
+def test_header_declarations_match_binding():
+    assert _declared_functions() == sorted(_native.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load_library()
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.b200_abi_version() == 100
+
+
+def test_plan_without_gpu_falls_back_to_148_sms():
+    # config 2: 256 x 8 units already fill the machine -> no split
+    plan = ops.plan_decode(256, 32, 8, 128, 16, 4096)
+    assert plan.num_parts == 1 and plan.workspace_bytes == 0
+    # config 5: 32 x 8 units of 32K tokens must be split
+    plan = ops.plan_decode(32, 32, 8, 128, 16, 32768)
+    assert plan.num_parts > 1 and plan.part_tokens * plan.num_parts >= 32768
+    assert plan.part_tokens % 16 == 0 and plan.part_tokens <= 8192
+    assert plan.workspace_bytes >= 32 * 32 * plan.num_parts * (128 + 1) * 4
+
+
+def test_forced_split_and_limits():
+    plan = ops.plan_decode(4, 8, 2, 128, 16, 1000, force_num_parts=5)
+    assert plan.num_parts == 5 and plan.part_tokens * 5 >= 1000
+    with pytest.raises(ValueError, match="8192"):
+        ops.plan_decode(4, 8, 2, 128, 16, 40000, force_num_parts=2)
+    with pytest.raises(RuntimeError, match="head_dim"):
+        ops.plan_decode(4, 8, 2, 64, 16, 1000)
+    with pytest.raises(RuntimeError, match="block_size"):
+        ops.plan_decode(4, 8, 2, 128, 8, 1000)
+
+
+def test_decode_rejects_malformed_arguments_before_launch():
+    lib = _native.load_library()
+    cache = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                               16 * 8 * 128, 8 * 128, 128)
+    plan = _native.DecodePlan(1, 4096, 0)
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, cache, 0x4000, 256, 0x5000, 4, 32,
+                               0x6000, 32 * 128, 128, 0.088, None, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT
+    assert b"plan" in lib.b200_last_error()
+    bad = _native.PagedCache(0x1008, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                             16 * 8 * 128, 8 * 128, 128)
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, bad, 0x4000, 256, 0x5000, 4, 32,
+                               0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT
+    assert b"16-byte aligned" in lib.b200_last_error()
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, cache, 0x4000, 256, 0x5000, 4, 36,
+                               0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT  # 36 % 8 != 0
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, cache, 0x4000, 256, 0x5000, 4, 256,
+                               0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
+    assert rc == _native.B200_ERR_UNSUPPORTED  # 32 q heads per KV head
+    split = _native.DecodePlan(4, 1024, 1 << 20)
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, cache, 0x4000, 256, 0x5000, 4, 32,
+                               0x6000, 32 * 128, 128, 0.088, split, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.b200_last_error()
+
+
+def test_prefill_and_append_reject_unsupported_shapes():
+    lib = _native.load_library()
+    cache = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 64, _native.DTYPE_BFLOAT16,
+                               16 * 8 * 64, 8 * 64, 64)
+    rc = lib.b200_paged_prefill(0x3000, 32 * 64, 64, cache, 0x4000, 2, 0x5000, 0x6000, 2, 10,
+                                5, 32, 0x7000, 32 * 64, 64, 0.125, None, None)
+    assert rc == _native.B200_ERR_UNSUPPORTED
+    rc = lib.b200_store_kvcache(0x1000, 1024, 0x2000, 1024, 0x3000, 0x4000, 1024, 0x5000, 0,
+                                4, 1024, 1, 64, None, None)
+    assert rc == _native.B200_ERR_UNSUPPORTED  # 1-byte elements
+    rc = lib.b200_store_kvcache(0x1000, 512, 0x2000, 1024, 0x3000, 0x4000, 1024, 0x5000, 0,
+                                4, 1024, 2, 64, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT  # stride shorter than a row
+    # zero tokens is a successful no-op, even with NULL pointers
+    assert lib.b200_store_kvcache(None, 1024, None, 1024, None, None, 1024, None, 0, 0, 1024,
+                                  2, 64, None, None) == _native.B200_OK
+
+
+def test_status_description():
+    assert _native.describe_status(0) == "ok"
+    text = _native.describe_status(_native.STATUS_WAIT_TIMEOUT | _native.STATUS_PAGE_OUT_OF_RANGE)
+    assert "timed out" in text and "page" in text
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIBRARY_PATH", tmp_path / "absent.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        _native.load_library()
+    assert not _native.library_available()
+    assert isinstance(ctypes.c_int32(0), ctypes.c_int32)
