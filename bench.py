@@ -210,7 +210,7 @@ def cpu_baseline_leg(sample_seqs):
     bytes_per_run = w.kv_bytes_read() + w.append_bytes()
     time_oracle(w, threads)  # warm
     runs, elapsed = 0, 0.0
-    while elapsed < 10.0 and runs < 20:
+    while elapsed < 10.0 and runs < 500:
         elapsed += time_oracle(w, threads)
         runs += 1
     gbs = bytes_per_run * runs / elapsed / 1e9
