@@ -147,6 +147,37 @@ B200_API int b200_paged_decode(const void* q, int64_t q_seq_stride, int64_t q_he
                       int64_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * Split-KV paged decode that allocates nothing. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory, such
+ * as a serving process that reserved nearly all of HBM for its KV pool at
+ * start-up and forbids later cudaMalloc calls, or a plugin host that owns
+ * every device allocation through its own pool and exposes no allocator
+ * across this ABI. Same arguments and result as b200_paged_decode without
+ * the workspace: the split-KV partials live in a fixed scratch array built
+ * into the library, B200_NOALLOC_DECODE_SCRATCH_BYTES per device, held by
+ * every GPU that loads the library until the process exits.
+ *   - A batch whose partials need more than that (num_seqs * num_q_heads *
+ *     plan->num_parts * 516 bytes, rounded up) is rejected with
+ *     B200_ERR_INVALID_ARGUMENT before anything is launched.
+ *   - The first call on a device looks up that device's scratch address
+ *     (cudaGetSymbolAddress, with the device current); make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one scratch array, which keeps the
+ *     last call's contents. Calls that overlap on the GPU (other streams,
+ *     other host threads) race on it: serialise them.
+ *   - No cudaMalloc, cudaFree or other allocating routine is called.
+ */
+#define B200_NOALLOC_DECODE_SCRATCH_BYTES (16u << 20) /* 16 MiB */
+B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_seq_stride,
+                                       int64_t q_head_stride, const b200_paged_cache* cache,
+                                       const int32_t* block_tables,
+                                       int64_t block_table_stride, const int32_t* seq_lens,
+                                       int32_t num_seqs, int32_t num_q_heads, void* out,
+                                       int64_t out_seq_stride, int64_t out_head_stride,
+                                       float softmax_scale, const b200_decode_plan* plan,
+                                       int32_t* status, void* stream);
+
+/*
  * Paged prefill / chunked-prefill attention over prefix-cached plus new
  * tokens. Sequence s owns query rows [query_start_loc[s], query_start_loc[s+1])
  * of q/out and seq_lens[s] KV tokens (the new ones included, already

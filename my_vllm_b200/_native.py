@@ -27,6 +27,10 @@ STATUS_PLAN_EXCEEDED = 0x10
 DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
 
+# Size of the scratch array built into the library for
+# b200_paged_decode_noalloc (B200_NOALLOC_DECODE_SCRATCH_BYTES).
+NOALLOC_DECODE_SCRATCH_BYTES = 16 << 20
+
 # Every symbol the header declares; tests check the library exports them all.
 EXPORTED_SYMBOLS = (
     "b200_abi_version",
@@ -35,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode_plan",
     "b200_paged_decode",
     "b200_paged_prefill",
+    "b200_paged_decode_noalloc",
 )
 
 
@@ -88,6 +93,13 @@ _SIGNATURES = {
         [
             _VP, _I64, _I64, ctypes.POINTER(PagedCache), _VP, _I64, _VP, _I32, _I32,
             _VP, _I64, _I64, _F32, ctypes.POINTER(DecodePlan), _VP, _I64, _VP, _VP,
+        ],
+        _I32,
+    ),
+    "b200_paged_decode_noalloc": (
+        [
+            _VP, _I64, _I64, ctypes.POINTER(PagedCache), _VP, _I64, _VP, _I32, _I32,
+            _VP, _I64, _I64, _F32, ctypes.POINTER(DecodePlan), _VP, _VP,
         ],
         _I32,
     ),

@@ -24,6 +24,7 @@ SOURCES = (
     "paged_decode.cu",
     "paged_prefill.cu",
     "capi.cu",
+    "paged_decode_noalloc.cu",
 )
 
 NVCC_FLAGS = (

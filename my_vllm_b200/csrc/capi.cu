@@ -165,6 +165,10 @@ int64_t decode_workspace_bytes(int64_t num_seqs, int64_t num_q_heads, int64_t nu
 
 }  // namespace
 
+namespace b200 {
+void set_last_error(const std::string& message) { g_last_error = message; }
+}  // namespace b200
+
 extern "C" {
 
 int b200_abi_version(void) { return 100; }
