@@ -50,6 +50,9 @@ def parse_args():
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="smaller batches are for profiler captures only")
+    ap.add_argument("--workload", choices=("config2", "config3"), default="config2",
+                    help="config3: mixed chunked prefill + decode (1 GPU), reports the "
+                         "prefill kernel against the tensor roofline")
     return ap.parse_args()
 
 
@@ -431,6 +434,99 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def visible_pairs(q_len, kv_len):
+    """Query-key pairs a causal chunk of q_len queries on kv_len keys sees."""
+    return q_len * (kv_len - q_len) + q_len * (q_len + 1) // 2
+
+
+def run_config3(args):
+    """Config 3 (mixed chunked prefill + decode) on one GPU: the step is the
+    engine's MIXED route — append 2172 rows, prefill rows [0, 2048) on the
+    tcgen05 kernel, decode rows [2048, 2172) — timed per kernel."""
+    from my_vllm_b200 import B200PagedBackend, ops, workloads
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    w = workloads.config3(device=device)
+    backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, BLOCK_SIZE,
+                               torch.bfloat16)
+    common = w.common_metadata()
+    plan = backend.build_plan(common)
+    md = plan.metadata
+    nP, P = common.num_prefill_seqs, common.num_prefill_tokens
+    out = torch.empty_like(w.q)
+    qsl, lens = w.extra["qsl_host"], w.extra["seq_lens_host"]
+    flops = sum(4 * w.num_q_heads * HEAD_DIM * visible_pairs(qsl[i + 1] - qsl[i], lens[i])
+                for i in range(nP))
+    es = w.k_cache.element_size()
+    prefill_kv_bytes = sum(lens[:nP]) * w.num_kv_heads * HEAD_DIM * es * 2
+    decode_kv_bytes = sum(lens[nP:]) * w.num_kv_heads * HEAD_DIM * es * 2
+    step_bytes = prefill_kv_bytes + decode_kv_bytes + w.append_bytes()
+    stream = torch.cuda.current_stream(device)
+
+    def prefill():
+        ops.paged_prefill(w.q[:P], w.k_cache, w.v_cache, md.block_tables[:nP],
+                          md.seq_lens[:nP], md.query_start_loc[: nP + 1], out[:P],
+                          common.max_q_len, backend.softmax_scale, num_seqs=nP)
+
+    def decode():
+        ops.paged_decode(w.q[P:], w.k_cache, w.v_cache, md.block_tables[nP:],
+                         md.seq_lens[nP:], out[P:], md.decode_plan, backend.softmax_scale,
+                         backend._workspace)
+
+    for _ in range(max(3, args.warmup)):
+        ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+        prefill()
+        decode()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+        ev[i][0].record(stream)
+        prefill()
+        ev[i][1].record(stream)
+        ev[i][2].record(stream)
+        decode()
+        ev[i][3].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    pre_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    dec_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    try:
+        peaks_data = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        tflops_peak, src = float(peaks_data["bf16_tflops"]), "measured burst cuBLAS bf16"
+    except (OSError, KeyError, ValueError):
+        tflops_peak, src = 1590.0, "fallback"
+    hbm, hbm_src = peaks()
+    pre_tf = flops / (pre_ms * 1e-3) / 1e12
+    dec_gbs = decode_kv_bytes / (dec_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC + " (config 3 mixed step)", "value": round(step_bytes / (ms * 1e-3) / 1e9, 2),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3: 4 x 512-token prefill chunks on shared prefix hits "
+                               "0/512/1024/2048 + 124 decode rows ctx U[128, 8192], Qwen3-8B "
+                               "heads, bs 16; append 2172 rows",
+                   "l2": "decode streams 2.1 GB per step between prefill launches"},
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel",
+                     "achieved": round(dec_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(dec_gbs / hbm, 4), "launch_ms": round(dec_ms, 5),
+                     "algorithmic_bytes_per_launch": decode_kv_bytes},
+        "roofline_prefill": {"bound": "tensor", "kernel": "paged_prefill_tc_kernel",
+                             "achieved": round(pre_tf, 1), "peak": tflops_peak,
+                             "unit": "TFLOP/s", "frac": round(pre_tf / tflops_peak, 4),
+                             "peak_source": src, "launch_ms": round(pre_ms, 5),
+                             "algorithmic_flops_per_launch": flops},
+        "gpu_launches": 3 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -438,6 +534,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "config3":
+        run_config3(args)
         return
     if world != args.gpus and "WORLD_SIZE" not in os.environ:
         world = args.gpus

@@ -23,6 +23,7 @@ SOURCES = (
     "kv_append.cu",
     "paged_decode.cu",
     "paged_prefill.cu",
+    "paged_prefill_tc.cu",
     "capi.cu",
     "paged_decode_noalloc.cu",
 )

@@ -338,10 +338,11 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
     return fail(B200_ERR_INVALID_ARGUMENT, "num_q_heads must be divisible by num_kv_heads");
   const int group = num_q_heads / cache->num_kv_heads;
   if (max_q_len <= 0) return fail(B200_ERR_INVALID_ARGUMENT, "max_q_len must be positive");
-  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 3) ||
-      (q_token_stride | q_head_stride | out_token_stride | out_head_stride) & 1)
+  if (group > 128) return fail(B200_ERR_UNSUPPORTED, "at most 128 q heads per KV head");
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15) ||
+      (q_token_stride | q_head_stride | out_token_stride | out_head_stride) & 7)
     return fail(B200_ERR_INVALID_ARGUMENT,
-                "q/out must be 4-byte aligned with even strides");
+                "q/out must be 16-byte aligned with strides that are multiples of 8");
   CUtensorMap mk, mv;
   if ((rc = cache_tensor_map(cache->k_cache, *cache, &mk)) != B200_OK) return rc;
   if ((rc = cache_tensor_map(cache->v_cache, *cache, &mv)) != B200_OK) return rc;
@@ -363,8 +364,8 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.status = status;
   cudaError_t e =
-      b200::launch_paged_prefill(mk, mv, p, cache->dtype, cache->num_kv_heads, num_seqs,
-                                 max_q_len, static_cast<cudaStream_t>(stream));
+      b200::launch_paged_prefill_tc(mk, mv, p, cache->dtype, cache->num_kv_heads, num_seqs,
+                                    max_q_len, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged prefill launch");
   return B200_OK;
 }

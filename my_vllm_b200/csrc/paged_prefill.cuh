@@ -34,4 +34,9 @@ cudaError_t launch_paged_prefill(const CUtensorMap& mk, const CUtensorMap& mv,
                                  const PrefillParams& p, int dtype, int num_kv_heads,
                                  int num_seqs, int max_q_len, cudaStream_t stream);
 
+// tcgen05 / TMEM version: 128 packed rows per CTA on UMMA M = 128 tiles.
+cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
+                                    const PrefillParams& p, int dtype, int num_kv_heads,
+                                    int num_seqs, int max_q_len, cudaStream_t stream);
+
 }  // namespace b200
