@@ -22,7 +22,6 @@ LIBRARY_PATH = PACKAGE_DIR / LIBRARY_NAME
 SOURCES = (
     "kv_append.cu",
     "paged_decode.cu",
-    "paged_prefill.cu",
     "paged_prefill_tc.cu",
     "capi.cu",
     "paged_decode_noalloc.cu",

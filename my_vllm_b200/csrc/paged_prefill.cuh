@@ -26,15 +26,9 @@ struct PrefillParams {
   int32_t* status;
 };
 
-// Rows of one CTA: (query token, q head of the group) pairs, packed so the
-// GQA heads of a KV head share every K/V tile the CTA loads.
-int prefill_rows_per_cta();
-
-cudaError_t launch_paged_prefill(const CUtensorMap& mk, const CUtensorMap& mv,
-                                 const PrefillParams& p, int dtype, int num_kv_heads,
-                                 int num_seqs, int max_q_len, cudaStream_t stream);
-
-// tcgen05 / TMEM version: 128 packed rows per CTA on UMMA M = 128 tiles.
+// tcgen05 / TMEM prefill: 128 packed (query token, q head of the group) rows
+// per CTA on UMMA M = 128 tiles, so the GQA heads of a KV head share every
+// K/V tile the CTA loads.
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
                                     const PrefillParams& p, int dtype, int num_kv_heads,
                                     int num_seqs, int max_q_len, cudaStream_t stream);
