@@ -123,6 +123,15 @@ class ClockSampler:
                 "samples": len(in_window), "when": note}
 
 
+def physical_gpu_indices(world):
+    """nvidia-smi indices of the GPUs the ranks use (CUDA_VISIBLE_DEVICES aware)."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in visible.split(",") if v.strip()]
+    if ids and all(v.isdigit() for v in ids):
+        return [int(v) for v in ids[:world]]
+    return list(range(world))
+
+
 # ---------------------------------------------------------------- workload --
 def make_shard(rank, world, device, batch=BATCH):
     from my_vllm_b200 import workloads
@@ -294,7 +303,7 @@ def run_ours(args, rank, world, local_rank):
 
     sampler = None
     if rank == 0 and not args.no_clocks:
-        sampler = ClockSampler(range(world))
+        sampler = ClockSampler(physical_gpu_indices(world))
         sampler.start()
 
     for _ in range(max(3, args.warmup)):
