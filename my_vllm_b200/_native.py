@@ -86,7 +86,7 @@ _SIGNATURES = {
         _I32,
     ),
     "b200_paged_decode_plan": (
-        [_I32, _I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(DecodePlan)],
+        [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32, ctypes.POINTER(DecodePlan)],
         _I32,
     ),
     "b200_paged_decode": (

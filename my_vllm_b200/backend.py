@@ -12,7 +12,10 @@ Lifecycle (nanovllm/layers/attention_backend.py:174-275):
   * ``forward(q, k, v, k_cache, v_cache, plan)`` writes every route into one
     backend-owned output buffer that is reused across layers (:905-920);
     MIXED_SPLIT writes rows [0, P) with the prefill kernel and rows [P, T)
-    with the decode kernel, without concatenation (:1011-1026).
+    with the decode kernel, without concatenation (:1011-1026), the two
+    kernels running concurrently on two streams.
+  * Full-decode CUDA Graphs (:242-275): fixed-address metadata buffers per
+    batch bucket, refreshed by ``plan_full_decode_graph`` before each replay.
 """
 
 from __future__ import annotations
@@ -51,6 +54,28 @@ class B200PagedMetadata:
     @property
     def is_cacheless(self) -> bool:
         return self.block_tables is None
+
+
+@dataclass
+class B200DecodeGraphState:
+    """Fixed-address buffers of one full-decode CUDA Graph bucket.
+
+    The graph bakes in device addresses, so the decode kernel reads its
+    metadata from these buffers; ``plan_full_decode_graph`` refreshes them
+    before every replay. The split-KV partition is planned once for the
+    bucket's worst case (every request at ``max_kv_len``) and never changes.
+    """
+
+    batch_size: int
+    max_pages: int
+    max_kv_len: int
+    query_start_loc: torch.Tensor  # int32 [B + 1]
+    seq_lens: torch.Tensor         # int32 [B]
+    block_tables: torch.Tensor     # int32 [B, max_pages]
+    output: torch.Tensor           # [B, Hq, D]
+    decode_plan: ops.DecodePlan
+    workspace: torch.Tensor | None
+    plan: AttentionPlan | None = None
 
 
 def validate_common_metadata(common: CommonAttentionMetadata, *, require_cuda: bool) -> None:
@@ -162,7 +187,7 @@ class B200PagedBackend(AttentionBackend):
     """Paged KV attention on hand-written sm_100a kernels (TMA + tensor cores)."""
 
     backend_name = BACKEND_NAME
-    supports_full_decode_graph = False
+    supports_full_decode_graph = True
 
     def __init__(
         self,
@@ -190,6 +215,8 @@ class B200PagedBackend(AttentionBackend):
         self._output_buffer: torch.Tensor | None = None
         self._workspace: torch.Tensor | None = None
         self._status: torch.Tensor | None = None
+        self._active_graph_state: B200DecodeGraphState | None = None
+        self._side_streams: dict[torch.device, torch.cuda.Stream] = {}
 
     # ------------------------------------------------------------ capability --
     @classmethod
@@ -259,6 +286,7 @@ class B200PagedBackend(AttentionBackend):
             decode_plan = ops.plan_decode(
                 common.num_decode_seqs, self.num_q_heads, self.num_kv_heads, self.head_dim,
                 self.block_size, self._decode_max_kv_len(common), self.decode_num_parts,
+                total_kv_tokens=self._decode_total_kv_tokens(common),
             )
         return B200PagedMetadata(
             common.query_start_loc, common.seq_lens, common.block_tables, decode_plan
@@ -278,6 +306,14 @@ class B200PagedBackend(AttentionBackend):
             # Untrusted metadata without host bounds: one read is the price.
             bound = int(common.seq_lens[common.num_prefill_seqs:].max().item())
         return bound
+
+    def _decode_total_kv_tokens(self, common: CommonAttentionMetadata) -> int:
+        """Upper bound of the decode rows' KV tokens from the host block counts
+        (0 when the metadata carries none)."""
+        counts = common.block_counts
+        if isinstance(counts, tuple) and len(counts) == common.num_seqs and counts:
+            return sum(counts[common.num_prefill_seqs:]) * self.block_size
+        return 0
 
     def build_plan(
         self, common: CommonAttentionMetadata, metadata: B200PagedMetadata | None = None
@@ -343,6 +379,19 @@ class B200PagedBackend(AttentionBackend):
             raise ValueError("key and value caches must both be present or absent")
         common = plan.common
 
+        graph_state = self._active_graph_state
+        if graph_state is not None:
+            if not has_k:
+                raise RuntimeError("full decode graph requires allocated KV cache")
+            self._validate_inputs(q, k_cache, v_cache)
+            if graph_state.output.shape != q.shape:
+                raise RuntimeError("decode graph attention output does not match query shape")
+            return ops.paged_decode(
+                q, k_cache, v_cache, graph_state.block_tables, graph_state.seq_lens,
+                graph_state.output, graph_state.decode_plan, self.softmax_scale,
+                graph_state.workspace, status=self.status_tensor(q.device),
+            )
+
         if plan.route is AttentionRoute.WARMUP or not has_k:
             if has_k:
                 raise ValueError("warmup route requires an empty KV cache")
@@ -374,20 +423,138 @@ class B200PagedBackend(AttentionBackend):
         if plan.batch_type is not expected:
             raise ValueError("B200 route does not match the planned BatchType")
 
-        if nP:
+        def prefill():
             ops.paged_prefill(
                 q[:P], k_cache, v_cache, block_tables[:nP], metadata.seq_lens[:nP],
                 metadata.query_start_loc[: nP + 1], output[:P], common.max_q_len,
                 self.softmax_scale, num_seqs=nP, status=status,
             )
-        if common.num_decode_seqs:
+
+        def decode():
             assert metadata.decode_plan is not None
             ops.paged_decode(
                 q[P:], k_cache, v_cache, block_tables[nP:], metadata.seq_lens[nP:],
                 output[P:], metadata.decode_plan, self.softmax_scale, self._workspace,
                 status=status,
             )
+
+        if nP and common.num_decode_seqs:
+            # MIXED: the decode kernel is HBM-bound and the prefill kernel
+            # tensor-bound, so they run concurrently: decode first on the
+            # caller's stream (its CTAs claim the SMs first), prefill on a side
+            # stream that joins back before returning. Rows are disjoint.
+            main = torch.cuda.current_stream(q.device)
+            side = self._side_stream(q.device)
+            side.wait_stream(main)
+            decode()
+            with torch.cuda.stream(side):
+                prefill()
+            main.wait_stream(side)
+        elif nP:
+            prefill()
+        else:
+            decode()
         return output
+
+    def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        stream = self._side_streams.get(device)
+        if stream is None:
+            stream = torch.cuda.Stream(device=device)
+            self._side_streams[device] = stream
+        return stream
+
+    # ------------------------------------------------- full-decode CUDA Graph --
+    # Lifecycle of attention_backend.py:242-275 (FlashInfer's :1028-1225):
+    # ModelRunner creates one state per batch bucket, plans it with the capture
+    # metadata, activates it while the model is captured, and before every
+    # replay calls plan_full_decode_graph with the step's real metadata.
+    def create_full_decode_graph_state(
+        self, batch_size: int, page_indices_capacity: int, device: torch.device | str
+    ) -> B200DecodeGraphState:
+        if isinstance(batch_size, bool) or not isinstance(batch_size, int):
+            raise TypeError("batch_size must be an int")
+        if isinstance(page_indices_capacity, bool) or not isinstance(page_indices_capacity, int):
+            raise TypeError("page_indices_capacity must be an int")
+        if batch_size <= 0 or page_indices_capacity < batch_size:
+            raise ValueError("graph state requires positive batch and page capacity")
+        graph_device = torch.device(device)
+        if graph_device.type != "cuda":
+            raise ValueError("full decode graph state must be on CUDA")
+        max_pages = (page_indices_capacity + batch_size - 1) // batch_size
+        max_kv_len = max_pages * self.block_size
+        decode_plan = ops.plan_decode(batch_size, self.num_q_heads, self.num_kv_heads,
+                                      self.head_dim, self.block_size, max_kv_len,
+                                      self.decode_num_parts)
+        workspace = None
+        if decode_plan.workspace_bytes:
+            workspace = torch.empty(decode_plan.workspace_bytes, dtype=torch.uint8,
+                                    device=graph_device)
+        return B200DecodeGraphState(
+            batch_size=batch_size,
+            max_pages=max_pages,
+            max_kv_len=max_kv_len,
+            query_start_loc=torch.arange(batch_size + 1, dtype=torch.int32, device=graph_device),
+            seq_lens=torch.ones(batch_size, dtype=torch.int32, device=graph_device),
+            block_tables=torch.zeros(batch_size, max_pages, dtype=torch.int32,
+                                     device=graph_device),
+            output=torch.empty(batch_size, self.num_q_heads, self.head_dim, dtype=self.dtype,
+                               device=graph_device),
+            decode_plan=decode_plan,
+            workspace=workspace,
+        )
+
+    def full_decode_graph_metadata_fits(self, state: Any, plan: AttentionPlan) -> bool:
+        if not isinstance(state, B200DecodeGraphState) or not isinstance(plan, AttentionPlan):
+            return False
+        if plan.batch_type is not BatchType.PURE_DECODE or plan.route is not AttentionRoute.DECODE:
+            return False
+        metadata = plan.metadata
+        if not isinstance(metadata, B200PagedMetadata) or metadata.block_tables is None:
+            return False
+        common = plan.common
+        if common.num_prefill_seqs or common.num_prefill_tokens:
+            return False
+        if common.num_decode_seqs != state.batch_size or common.num_decode_tokens != state.batch_size:
+            return False
+        tables = metadata.block_tables
+        tensors = (metadata.query_start_loc, metadata.seq_lens, common.slot_mapping)
+        if any(not isinstance(t, torch.Tensor) or t.dtype != torch.int32
+               or t.device.type != "cuda" or t.ndim != 1 for t in tensors):
+            return False
+        if metadata.query_start_loc.numel() != state.batch_size + 1:
+            return False
+        if metadata.seq_lens.numel() != state.batch_size:
+            return False
+        if common.slot_mapping.numel() != state.batch_size:
+            return False
+        if (tables.dtype != torch.int32 or tables.device.type != "cuda" or tables.ndim != 2
+                or tables.size(0) != state.batch_size or tables.size(1) > state.max_pages):
+            return False
+        if common.max_kv_len > state.max_kv_len:
+            return False
+        return True
+
+    def plan_full_decode_graph(self, state: Any, plan: AttentionPlan) -> None:
+        if not self.full_decode_graph_metadata_fits(state, plan):
+            raise ValueError("attention plan does not fit full decode graph state")
+        metadata = plan.metadata
+        width = metadata.block_tables.size(1)
+        state.query_start_loc.copy_(metadata.query_start_loc)
+        state.seq_lens.copy_(metadata.seq_lens)
+        state.block_tables[:, :width].copy_(metadata.block_tables)
+        state.plan = plan
+
+    def activate_full_decode_graph(self, state: Any) -> None:
+        if not isinstance(state, B200DecodeGraphState):
+            raise TypeError("invalid B200 decode graph state")
+        if state.plan is None:
+            raise RuntimeError("decode graph state must be planned before activation")
+        if self._active_graph_state is not None:
+            raise RuntimeError("a decode graph state is already active")
+        self._active_graph_state = state
+
+    def deactivate_full_decode_graph(self) -> None:
+        self._active_graph_state = None
 
     def _validate_inputs(self, q, k_cache, v_cache) -> None:
         if q.device.type != "cuda" or q.dtype != self.dtype:
@@ -428,6 +595,7 @@ def register(registry=AttentionBackendRegistry, name: str = BACKEND_NAME) -> Non
 
 
 __all__ = [
+    "B200DecodeGraphState",
     "B200PagedBackend",
     "B200PagedMetadata",
     "classify_batch",

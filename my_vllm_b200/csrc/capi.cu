@@ -202,7 +202,8 @@ int b200_store_kvcache(const void* key, int64_t key_row_stride, const void* valu
 
 int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t head_dim, int32_t block_size, int32_t max_kv_len,
-                           int32_t force_num_parts, b200_decode_plan* plan) {
+                           int64_t total_kv_tokens, int32_t force_num_parts,
+                           b200_decode_plan* plan) {
   g_last_error.clear();
   if (plan == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "plan is NULL");
   if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
@@ -229,6 +230,19 @@ int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv
     const int64_t units = (int64_t)num_seqs * num_kv_heads;
     const int64_t slots = (int64_t)sm_count() * b200::decode_ctas_per_sm();
     parts = min_parts;
+    // Ragged batches: no CTA should hold more than a quarter of the average
+    // per-slot work, or the longest sequences finish last on a few SMs.
+    const int64_t max_tokens = (int64_t)num_seqs * max_kv_len;
+    const int64_t total = (total_kv_tokens > 0 && total_kv_tokens < max_tokens)
+                              ? total_kv_tokens : max_tokens;
+    if (total < max_tokens) {
+      const int64_t total_tiles = (total + b200::kTileTokens - 1) / b200::kTileTokens;
+      const double per_slot = double(total_tiles) * num_kv_heads / double(slots);
+      int64_t balance = (int64_t)(4.0 * double(tiles) / per_slot + 0.999999);
+      const int64_t cap = tiles / 4 > 1 ? tiles / 4 : 1;  // >= 4 tiles per partition
+      if (balance > cap) balance = cap;
+      if (balance > parts) parts = balance;
+    }
     if (units * parts < 2 * slots) {
       int64_t best = parts;
       double best_eff = 0.0;

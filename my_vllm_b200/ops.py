@@ -125,12 +125,14 @@ def plan_decode(
     block_size: int,
     max_kv_len: int,
     force_num_parts: int = 0,
+    total_kv_tokens: int = 0,
 ) -> DecodePlan:
-    """Choose the split-KV partition for a decode batch (host only, no sync)."""
+    """Choose the split-KV partition for a decode batch (host only, no sync).
+    ``total_kv_tokens`` (0 = unknown) lets the planner balance ragged batches."""
     plan = _native.DecodePlan()
     rc = _native.load_library().b200_paged_decode_plan(
         num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max(1, max_kv_len),
-        force_num_parts, plan,
+        int(total_kv_tokens), force_num_parts, plan,
     )
     _native.check(rc, "b200_paged_decode_plan")
     return DecodePlan(*plan.as_tuple())

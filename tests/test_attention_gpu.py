@@ -223,3 +223,59 @@ def test_warmup_route_without_cache(cuda_device):
     ref = oracle.paged_attention_from_tables(storage(q), kc, vc, [[0], [1]], [3, 1], [0, 3, 4],
                                              16, out_dtype="float32")
     assert_close_to_oracle(out, ref, torch.bfloat16)
+
+
+def test_full_decode_cuda_graph_replay(cuda_device):
+    """The engine's full-decode graph flow (model_runner.py:676-766): capture the
+    append + attention with slot -1 on page 0, then replay with real metadata."""
+    w = workloads.config2(device=cuda_device, batch=8, ctx=700, pool_blocks=512)
+    backend = _backend(w)
+    eager, plan = _append_and_run(w, backend, cuda_device)
+    expected, rows = sample_oracle(w, list(range(8)))
+
+    state = backend.create_full_decode_graph_state(8, 8 * 64, cuda_device)
+    static_q = torch.zeros_like(w.q)
+    static_k = torch.zeros_like(w.key)
+    static_v = torch.zeros_like(w.value)
+    static_slots = torch.full((8,), -1, dtype=torch.int32, device=cuda_device)
+    capture_common = CommonAttentionMetadata(
+        num_prefill_seqs=0, num_decode_seqs=8, num_prefill_tokens=0, num_decode_tokens=8,
+        query_start_loc=torch.arange(9, dtype=torch.int32, device=cuda_device),
+        seq_lens=torch.ones(8, dtype=torch.int32, device=cuda_device),
+        slot_mapping=static_slots,
+        block_tables=torch.zeros(8, 1, dtype=torch.int32, device=cuda_device),
+        max_q_len=1, max_kv_len=1, block_counts=(1,) * 8, num_kv_blocks=8, trusted=True)
+    capture_plan = backend.build_plan(capture_common)
+    page0 = (w.k_cache[0].clone(), w.v_cache[0].clone())
+    backend.plan_full_decode_graph(state, capture_plan)
+    backend.activate_full_decode_graph(state)
+    try:
+        def body():
+            ops.store_kvcache(static_k, static_v, w.k_cache, w.v_cache, static_slots)
+            return backend.forward(static_q, static_k, static_v, w.k_cache, w.v_cache,
+                                   capture_plan)
+        body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            graph_out = body()
+    finally:
+        backend.deactivate_full_decode_graph()
+    torch.cuda.synchronize()
+    # slot -1 rows never write, so the capture leaves page 0 untouched
+    assert torch.equal(w.k_cache[0].view(torch.int16), page0[0].view(torch.int16))
+    assert torch.equal(w.v_cache[0].view(torch.int16), page0[1].view(torch.int16))
+    assert graph_out.data_ptr() == state.output.data_ptr()
+
+    assert backend.full_decode_graph_metadata_fits(state, plan)
+    for _ in range(2):  # replay twice: the buffers are refreshed, not re-captured
+        backend.plan_full_decode_graph(state, plan)
+        static_q.copy_(w.q)
+        static_k.copy_(w.key)
+        static_v.copy_(w.value)
+        static_slots.copy_(w.slot_mapping)
+        graph.replay()
+        torch.cuda.synchronize()
+        backend.check_status()
+        assert_close_to_oracle(state.output[rows], expected, w.q.dtype)
+    assert (state.output.float() - eager.float()).abs().max().item() <= MAX_ABS[w.q.dtype]

@@ -57,7 +57,7 @@ def _metadata(backend, common):
 def test_constructor_rules():
     backend = B200PagedBackend(16, 4, 128, 16, torch.bfloat16)
     assert backend.softmax_scale == pytest.approx(128 ** -0.5)
-    assert backend.backend_name == "b200" and backend.supports_full_decode_graph is False
+    assert backend.backend_name == "b200" and backend.supports_full_decode_graph is True
     with pytest.raises(ValueError, match="block_size"):
         B200PagedBackend(16, 4, 128, 8, torch.bfloat16)
     with pytest.raises(ValueError, match="head_dim"):
@@ -191,3 +191,32 @@ def test_registry_register_and_create_errors():
     with pytest.raises(RuntimeError, match="unusable: a CUDA device is required"):
         Registry.create("b200-test", num_q_heads=32, num_kv_heads=8, head_dim=128,
                         block_size=16, dtype=torch.bfloat16)
+
+
+def test_ragged_batches_get_more_partitions_than_uniform_ones():
+    # 124 sequences, longest 8192: uniform lengths fill the machine without a
+    # split, but a ragged batch (average ~4160 tokens) is cut finer.
+    uniform = ops.plan_decode(124, 32, 8, 128, 16, 8192, total_kv_tokens=124 * 8192)
+    ragged = ops.plan_decode(124, 32, 8, 128, 16, 8192, total_kv_tokens=124 * 4160)
+    assert uniform.num_parts == 1
+    assert ragged.num_parts >= 3 and ragged.part_tokens * ragged.num_parts >= 8192
+    # unknown totals behave like uniform batches
+    assert ops.plan_decode(124, 32, 8, 128, 16, 8192).num_parts == uniform.num_parts
+
+
+def test_full_decode_graph_state_contract_without_gpu():
+    backend = B200PagedBackend(16, 4, 128, 16, torch.bfloat16)
+    with pytest.raises(TypeError):
+        backend.create_full_decode_graph_state(True, 8, "cuda")
+    with pytest.raises(TypeError):
+        backend.create_full_decode_graph_state(2, 8.0, "cuda")
+    with pytest.raises(ValueError, match="positive"):
+        backend.create_full_decode_graph_state(4, 2, "cuda")
+    with pytest.raises(ValueError, match="on CUDA"):
+        backend.create_full_decode_graph_state(2, 8, "cpu")
+    common = _common((1, 1), (21, 13), 0)
+    plan = backend.build_plan(common, _metadata(backend, common))
+    assert backend.full_decode_graph_metadata_fits(object(), plan) is False
+    with pytest.raises(TypeError):
+        backend.activate_full_decode_graph(object())
+    backend.deactivate_full_decode_graph()
