@@ -7,25 +7,30 @@
 // the new chunk, already appended). Query token i sits at KV position
 // seq_len - q_len + i and attends to positions <= that one.
 //
-// Design (one CTA per (sequence, KV head, block of 128 packed rows)):
-//   * A row is a (query token, q head of the GQA group) pair; 128 rows form
-//     the M = 128 side of every UMMA, so the group's heads share each K/V
-//     tile that crosses HBM/L2.
-//   * warps 0-3 (128 threads): softmax and epilogue, thread t owns row t =
-//     TMEM lane t, so row max / row sum need no shuffles. They stage Q into
-//     shared memory (K-major, 128-byte swizzle) at the start.
-//   * warp 4: TMA producer, 128-token K/V tiles of the paged cache (8 x
-//     16-token sub-tiles, one lane each) into a 2-stage ring.
-//   * warp 5: TMEM allocation (256 columns: S | O) and the single thread that
-//     issues tcgen05.mma: S = Q K^T (A, B K-major) into TMEM, then
-//     O += P V with P (bf16, written by the softmax warps into shared memory,
-//     K-major) and V read N-major straight from the TMA tile.
+// Design (one CTA per (sequence, KV head, block of 256 packed rows)):
+//   * A row is a (query token, q head of the GQA group) pair; the CTA's rows
+//     form two UMMA M = 128 tiles, A and B, that share every K/V tile.
+//   * warps 0-3 / 4-7: two softmax warpgroups, one per Q tile; thread t of a
+//     group owns row t = TMEM lane t, so row max and row sum need no shuffles.
+//     They stage their Q tile into shared memory (K-major, 128-byte swizzle).
+//   * warp 8: TMA producer streaming 128-token K/V tiles of the paged cache
+//     (8 x 16-token sub-tiles, one lane each) into a 2-stage ring.
+//   * warp 9: allocates all 512 TMEM columns (S_A | O_A | S_B | O_B) and one
+//     thread issues every tcgen05.mma. The order
+//        PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), PV_A(j+1), ...
+//     keeps the tensor core on one tile's MMAs while the other warpgroup runs
+//     its softmax (ping-pong), and because MMAs of one thread complete in
+//     order, "S_X(j) done" also means "PV_X(j-1) done": the softmax may then
+//     rescale O_X and overwrite S_X with P_X without further waits.
+//   * S = Q K^T with A = Q, B = K both K-major from shared memory. The softmax
+//     writes P (16-bit) over S in TMEM and O += P V reads A = P from tensor
+//     memory and B = V N-major straight from the TMA tile.
 //   * Online softmax in the exp2 domain with a lazy rescale: the running
-//     maximum only moves when a tile's maximum exceeds it by more than 2^8,
-//     so O (in TMEM) is rarely rescaled; O / l is independent of that choice.
+//     maximum only moves when a tile's maximum exceeds it by more than 2^8, so
+//     O (in TMEM) is rarely rescaled; O / l is independent of that choice.
 //   * The bottom-right causal mask and the sequence end are applied in
 //     registers; V rows past the sequence end are zeroed in shared memory
-//     before the last PV MMA (never-written cache slots may hold NaN).
+//     before the last PV MMAs (never-written cache slots may hold NaN).
 //   * Every mbarrier wait is bounded; on a timeout the CTA reports
 //     B200_STATUS_WAIT_TIMEOUT, drains its TMA loads and MMAs with bounded
 //     waits, frees its tensor memory and exits.
@@ -39,36 +44,25 @@
 
 namespace b200 {
 
-constexpr int kTcRows = 128;   // UMMA M
+constexpr int kTcRows = 128;   // UMMA M (rows of one Q tile)
+constexpr int kTcTiles = 2;    // Q tiles per CTA
 constexpr int kTcKv = 128;     // KV tokens per tile (N of QK^T, K of PV)
-constexpr int kTcThreads = 192;
-constexpr int kTcHalf = kTcRows * 128;           // [128 rows x 64 elements] = 16 KiB
-constexpr int kTcQ = 0;
-constexpr int kTcStage0 = 2 * kTcHalf;           // 32 KiB after Q
-constexpr int kTcStageBytes = 4 * kTcHalf;       // K lo/hi + V lo/hi = 64 KiB
-constexpr int kTcP = kTcStage0 + 2 * kTcStageBytes;
-constexpr int kTcBars = kTcP + 2 * kTcHalf;
-constexpr int kTcSmemBytes = 1024 + kTcBars + 128;
-constexpr uint32_t kTcTmemCols = 256;            // S: [0, 128), O: [128, 256)
-constexpr float kRescaleThreshold = 8.0f;        // log2 units
-
-__device__ __forceinline__ uint4 pack8(const float* v) {
-  uint4 r;
-  r.x = Elem<__nv_bfloat16>::pack(v[0], v[1]);
-  r.y = Elem<__nv_bfloat16>::pack(v[2], v[3]);
-  r.z = Elem<__nv_bfloat16>::pack(v[4], v[5]);
-  r.w = Elem<__nv_bfloat16>::pack(v[6], v[7]);
-  return r;
-}
+constexpr int kTcThreads = 320;
+constexpr int kTcProducerWarp = 8;
+constexpr int kTcMmaWarp = 9;
+constexpr int kTcHalf = kTcRows * 128;          // [128 rows x 64 elements] = 16 KiB
+constexpr int kTcQ = 0;                         // Q_A, Q_B: 2 x 32 KiB
+constexpr int kTcStage0 = kTcTiles * 2 * kTcHalf;
+constexpr int kTcStageBytes = 4 * kTcHalf;      // K lo/hi + V lo/hi = 64 KiB
+constexpr int kTcStages = 2;
+constexpr int kTcBars = kTcStage0 + kTcStages * kTcStageBytes;
+constexpr int kTcSmemBytes = 1024 + kTcBars + 256;
+constexpr uint32_t kTcTmemCols = 512;           // per tile X: S_X at 256X, O_X at 256X+128
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
 template <typename T>
-__device__ __forceinline__ uint4 pack8_t(const float* v) {
-  uint4 r;
-  r.x = Elem<T>::pack(v[0], v[1]);
-  r.y = Elem<T>::pack(v[2], v[3]);
-  r.z = Elem<T>::pack(v[4], v[5]);
-  r.w = Elem<T>::pack(v[6], v[7]);
-  return r;
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return Elem<T>::pack(lo, hi);
 }
 
 template <typename T>
@@ -80,14 +74,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBars);
-  // barrier slots
   uint64_t* kv_full = bars + 0;    // [2] TMA -> MMA
   uint64_t* kv_empty = bars + 2;   // [2] MMA (commit) -> TMA
-  uint64_t* s_full = bars + 4;     // MMA (commit) -> softmax
-  uint64_t* p_ready = bars + 5;    // softmax (128 arrivals) -> MMA
-  uint64_t* o_done = bars + 6;     // MMA (commit) -> softmax
-  uint64_t* mma_drain = bars + 7;  // MMA (commit) -> MMA, before TMEM is freed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* s_full = bars + 4;     // [2] per Q tile: MMA (commit) -> softmax
+  uint64_t* p_ready = bars + 6;    // [2] per Q tile: softmax (128 arrivals) -> MMA
+  uint64_t* o_done = bars + 8;     // [2] per Q tile: MMA (commit) -> epilogue
+  uint64_t* mma_drain = bars + 10; // MMA (commit) -> MMA, before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -99,48 +92,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int q_len = p.query_start_loc[s + 1] - q_start;
   const int seq_len = p.seq_lens[s];
   const int group = p.group;
-  const int tpc = kTcRows / group;  // query tokens per CTA
+  const int tpc = (kTcTiles * kTcRows) / group;  // query tokens per CTA
   const int tok_begin = rb * tpc;
   if (tok_begin >= q_len || seq_len <= 0) return;  // CTA-uniform, before any sync
   const int ctx = seq_len - q_len;
-  const int tok_last = min(q_len, tok_begin + tpc) - 1;
-  const int kv_limit = min(seq_len, max(1, ctx + tok_last + 1));
-  const int n_tiles = (kv_limit + kTcKv - 1) / kTcKv;
+
+  // KV tiles each Q tile needs: up to its last valid row's causal limit.
+  auto tiles_for = [&](int x) {
+    const int first_row = x * kTcRows;
+    if (first_row / group >= tpc || tok_begin + first_row / group >= q_len) return 0;
+    const int last_row = min((x + 1) * kTcRows, tpc * group) - 1;
+    const int last_tok = min(q_len - 1, tok_begin + last_row / group);
+    const int kv_limit = min(seq_len, max(1, ctx + last_tok + 1));
+    return (kv_limit + kTcKv - 1) / kTcKv;
+  };
+  const int n_a = tiles_for(0);
+  const int n_b = tiles_for(1);
+  const int n_total = max(n_a, n_b);  // tiles the producer streams
 
   const uint32_t sbase = smem_u32(smem);
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&kv_full[0]), 1);
-    mbar_init(smem_u32(&kv_full[1]), 1);
-    mbar_init(smem_u32(&kv_empty[0]), 1);
-    mbar_init(smem_u32(&kv_empty[1]), 1);
-    mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(p_ready), 128);
-    mbar_init(smem_u32(o_done), 1);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(smem_u32(&kv_full[i]), 1);
+      mbar_init(smem_u32(&kv_empty[i]), 1);
+    }
+    for (int x = 0; x < kTcTiles; ++x) {
+      mbar_init(smem_u32(&s_full[x]), 1);
+      mbar_init(smem_u32(&p_ready[x]), kTcRows);
+      mbar_init(smem_u32(&o_done[x]), 1);
+    }
     mbar_init(smem_u32(mma_drain), 1);
     mbar_init_fence();
   }
-  if (warp == 5) {
+  if (warp == kTcMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
     tmem_relinquish();
   }
 
   // ---- softmax warps: this thread's row and its Q into shared memory ----
-  const int t = threadIdx.x;
+  const int x_tile = warp >> 2;       // Q tile of a softmax warp (0 or 1)
+  const int t = threadIdx.x & 127;    // row within the Q tile = TMEM lane
   int row_token = -1, row_head = 0, qpos = -1;
-  if (warp < 4) {
-    const int tl = t / group;
+  if (warp < 8) {
+    const int r = x_tile * kTcRows + t;
+    const int tl = r / group;
     if (tl < tpc && tok_begin + tl < q_len) {
       row_token = tok_begin + tl;
-      row_head = kvh * group + (t - tl * group);
+      row_head = kvh * group + (r - tl * group);
       qpos = ctx + row_token;
     }
     const uint4* src = reinterpret_cast<const uint4*>(
         reinterpret_cast<const T*>(p.q) + (int64_t)(q_start + max(row_token, 0)) * p.q_token_stride +
         (int64_t)row_head * p.q_head_stride);
+    uint8_t* qtile = smem + kTcQ + x_tile * 2 * kTcHalf;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       const uint4 v = row_token >= 0 ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(smem + kTcQ + (c >> 3) * kTcHalf + swz128(t, c & 7)) = v;
+      *reinterpret_cast<uint4*>(qtile + (c >> 3) * kTcHalf + swz128(t, c & 7)) = v;
     }
     fence_proxy_async_smem();
   }
@@ -148,19 +156,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tS = tmem_base;
-  const uint32_t tO = tmem_base + 128;
   bool ok = true;
 
-  if (warp == 4) {
+  if (warp == kTcProducerWarp) {
     // ------------------------------------------------------------ producer --
     const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
     const int max_page_idx = (seq_len - 1) / p.block_size;
     int issued = 0;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (j >= 2) {
-        const bool got = mbar_wait(smem_u32(&kv_empty[st]), ((j >> 1) - 1) & 1);
+    for (int j = 0; j < n_total; ++j) {
+      const int st = j % kTcStages;
+      if (j >= kTcStages) {
+        const bool got = mbar_wait(smem_u32(&kv_empty[st]), ((j / kTcStages) - 1) & 1);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -190,10 +196,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (!ok) {
       if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
-      for (int j = max(0, issued - 2); j < issued; ++j)
-        mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1);
+      for (int j = max(0, issued - kTcStages); j < issued; ++j)
+        mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == kTcMmaWarp) {
     // ---------------------------------------------------------- MMA issuer --
     if (lane == 0) {
       constexpr bool kBf16 = Elem<T>::kDtype == B200_DTYPE_BFLOAT16;
@@ -202,44 +208,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       auto kmajor = [&](uint32_t addr, int k) {  // K-major, 16-element k-step k
         return smem_desc(addr + (k >> 2) * kTcHalf + (k & 3) * 32, 16, 1024);
       };
-      auto issue_pv = [&](int j) {
-        const uint32_t vbase = sbase + kTcStage0 + (j & 1) * kTcStageBytes + 2 * kTcHalf;
+      auto issue_s = [&](int x, int j) {
+        const uint32_t qbase = sbase + kTcQ + x * 2 * kTcHalf;
+        const uint32_t kbase = sbase + kTcStage0 + (j % kTcStages) * kTcStageBytes;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k)
+          umma_f16(tmem_base + x * 256, kmajor(qbase, k), kmajor(kbase, k), idesc_s,
+                   k > 0 ? 1u : 0u);
+        umma_commit(smem_u32(&s_full[x]));
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t vbase =
+            sbase + kTcStage0 + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf;
+        const uint32_t tP = tmem_base + x * 256;  // P (16-bit, packed) over S
 #pragma unroll
         for (int k = 0; k < kTcKv / 16; ++k)
-          umma_f16(tO, kmajor(sbase + kTcP, k),
-                   smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
-                   (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(smem_u32(o_done));
-        umma_commit(smem_u32(&kv_empty[j & 1]));
+          umma_f16_ts(tmem_base + x * 256 + 128, tP + k * 8,
+                      smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
+                      (j > 0 || k > 0) ? 1u : 0u);
       };
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(smem_u32(&kv_full[st]), (j >> 1) & 1)) {
+      int kv_ready = -1;  // highest tile whose kv_full phase was observed
+      auto wait_kv = [&](int j) {
+        if (j <= kv_ready) return true;
+        if (!mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1)) return false;
+        tc_fence_after_sync();
+        kv_ready = j;
+        return true;
+      };
+      // One Q tile's step j: PV of tile j, then S of tile j + 1.
+      auto step = [&](int x, int n_x, int j) {
+        if (j >= n_x) return true;
+        if (!mbar_wait(smem_u32(&p_ready[x]), j & 1)) return false;
+        tc_fence_after_sync();
+        issue_pv(x, j);
+        if (j == n_x - 1) umma_commit(smem_u32(&o_done[x]));
+        if (j + 1 < n_x) {
+          if (!wait_kv(j + 1)) return false;
+          issue_s(x, j + 1);
+        }
+        return true;
+      };
+      // prologue: S of tile 0 for both Q tiles
+      if (!wait_kv(0)) ok = false;
+      if (ok && n_a > 0) issue_s(0, 0);
+      if (ok && n_b > 0) issue_s(1, 0);
+      for (int j = 0; j < n_total && ok; ++j) {
+        if (!step(0, n_a, j) || !step(1, n_b, j)) {
           ok = false;
           break;
         }
-        tc_fence_after_sync();
-        if (j > 0) {
-          if (!mbar_wait(smem_u32(p_ready), (j - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-          issue_pv(j - 1);
-        }
-        const uint32_t kbase = sbase + kTcStage0 + st * kTcStageBytes;
-#pragma unroll
-        for (int k = 0; k < kHeadDim / 16; ++k)
-          umma_f16(tS, kmajor(sbase + kTcQ, k), kmajor(kbase, k), idesc_s, k > 0 ? 1u : 0u);
-        umma_commit(smem_u32(s_full));
-      }
-      if (ok) {
-        if (mbar_wait(smem_u32(p_ready), (n_tiles - 1) & 1)) {
-          tc_fence_after_sync();
-          issue_pv(n_tiles - 1);
-        } else {
-          ok = false;
-        }
+        umma_commit(smem_u32(&kv_empty[j % kTcStages]));  // after every reader of tile j
       }
       if (!ok) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
       // every MMA this thread issued has completed before TMEM is released
@@ -249,30 +267,48 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------- softmax warps --
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + x_tile * 256 + lane_off;
+    const uint32_t tO = tS + 128;
+    const int my_tiles = x_tile ? n_b : n_a;
     const float kNegInf = -INFINITY;
     float m_used = kNegInf, l = 0.f;
-    for (int j = 0; j < n_tiles; ++j) {
-      const bool got = mbar_wait(smem_u32(s_full), j & 1);
+    for (int j = 0; j < my_tiles; ++j) {
+      const bool got = mbar_wait(smem_u32(&s_full[x_tile]), j & 1);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after_sync();
-      float sv[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tS + lane_off + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
+      // S_X(j) done implies PV_X(j-1) done (in-order MMAs): O_X is stable and
+      // the P_X(j-1) columns may be overwritten. Two passes over the row in
+      // 32-column chunks (max, then exp2 + pack) keep register use low enough
+      // for 10 warps per SM; independent accumulators keep the few warps per
+      // SM sub-partition busy instead of waiting on one dependency chain.
       const int kbase = j * kTcKv;
-      const bool need_mask = kbase + kTcKv - 1 > qpos || kbase + kTcKv > seq_len;
-      float m_tile = kNegInf;
+      // columns [0, lim) of this tile are visible to this row
+      const int lim = min(qpos - kbase + 1, seq_len - kbase);
+      const bool need_mask = lim < kTcKv;
+      float mk[8];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float v = sv[i] * p.scale_log2;
-        if (need_mask && (kbase + i > qpos || kbase + i >= seq_len)) v = kNegInf;
-        sv[i] = v;
-        m_tile = fmaxf(m_tile, v);
+      for (int k = 0; k < 8; ++k) mk[k] = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld32(tS + c * 32, sv);
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            mk[i & 7] = fmaxf(mk[i & 7], c * 32 + i < lim ? sv[i] : kNegInf);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mk[i & 7] = fmaxf(mk[i & 7], sv[i]);
+        }
       }
+      // the softmax scale is positive, so it commutes with the maximum
+      const float m_raw = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
+                                fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
+      const float m_tile = m_raw == kNegInf ? kNegInf : m_raw * p.scale_log2;
       float alpha = 1.f;
       bool rescale = false;
       if (m_tile > m_used + kRescaleThreshold) {
@@ -280,84 +316,91 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         m_used = m_tile;
         rescale = true;
       }
-      const float base = m_used == kNegInf ? 0.f : m_used;
-      float sum = 0.f;
+      const float neg_base = m_used == kNegInf ? 0.f : -m_used;
+      const float scale = p.scale_log2;
+      float sk[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        const float pv = fast_exp2(sv[i] - base);
-        sv[i] = pv;
-        sum += pv;
-      }
-      l = l * alpha + sum;
-
-      if (j > 0) {
-        // PV of the previous tile must be done: it reads the P buffer and
-        // writes O.
-        const bool done = mbar_wait(smem_u32(o_done), (j - 1) & 1);
-        if (!__all_sync(0xffffffffu, done)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after_sync();
-        if (__any_sync(0xffffffffu, rescale)) {
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld32(tS + c * 32, sv);
+        uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            tmem_ld32(tO + lane_off + c * 32, ov);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(tO + lane_off + c * 32, ov);
+        for (int i = 0; i < 16; ++i) {
+          float p0 = ex2_approx(fmaf(sv[2 * i], scale, neg_base));
+          float p1 = ex2_approx(fmaf(sv[2 * i + 1], scale, neg_base));
+          if (need_mask) {
+            p0 = c * 32 + 2 * i < lim ? p0 : 0.f;
+            p1 = c * 32 + 2 * i + 1 < lim ? p1 : 0.f;
           }
-          tmem_wait_st();
+          sk[i & 3] += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        // P over S: chunk c's 32 values -> 16 columns at 16c, which only
+        // overlap S columns this row has already read
+        tmem_st16(tS + c * 16, pk);
+      }
+      const float sum = (sk[0] + sk[1]) + (sk[2] + sk[3]);
+      l = l * alpha + sum;
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tO + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tO + c * 32, ov);
         }
       }
       if (kbase + kTcKv > seq_len) {
-        // Last tile: V rows past the sequence end may hold never-written
-        // cache slots (possibly NaN) and P = 0 does not cancel NaN.
-        const bool landed = mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1);
+        // Last KV tile: V rows past the sequence end may hold never-written
+        // cache slots (possibly NaN) and P = 0 does not cancel NaN. Both
+        // warpgroups write the same zeros, each before its own PV.
+        const bool landed = mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1);
         if (!__all_sync(0xffffffffu, landed)) {
           ok = false;
           break;
         }
         if (kbase + t >= seq_len) {
-          uint8_t* vrow = smem + kTcStage0 + (j & 1) * kTcStageBytes + 2 * kTcHalf + t * 128;
+          uint8_t* vrow =
+              smem + kTcStage0 + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf + t * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
             *reinterpret_cast<uint4*>(vrow + kTcHalf + c * 16) = make_uint4(0, 0, 0, 0);
           }
         }
+        fence_proxy_async_smem();
       }
-      // P (16-bit) into shared memory, K-major, 128-byte swizzle
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        *reinterpret_cast<uint4*>(smem + kTcP + (c >> 3) * kTcHalf + swz128(t, c & 7)) =
-            pack8_t<T>(&sv[c * 8]);
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before_sync();
-      mbar_arrive(smem_u32(p_ready));
+      mbar_arrive(smem_u32(&p_ready[x_tile]));
     }
-    if (ok) {
-      const bool done = mbar_wait(smem_u32(o_done), (n_tiles - 1) & 1);
+    if (ok && my_tiles > 0) {
+      const bool done = mbar_wait(smem_u32(&o_done[x_tile]), 0);
       if (!__all_sync(0xffffffffu, done)) ok = false;
     }
     if (!ok) {
       if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
-    } else {
+    } else if (my_tiles > 0) {
       tc_fence_after_sync();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + max(row_token, 0)) * p.out_token_stride +
+      T* orow = reinterpret_cast<T*>(p.out) +
+                (int64_t)(q_start + max(row_token, 0)) * p.out_token_stride +
                 (int64_t)row_head * p.out_head_stride;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float ov[32];
-        tmem_ld32(tO + lane_off + c * 32, ov);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] *= inv_l;
+        tmem_ld32(tO + c * 32, ov);
         if (row_token >= 0) {
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8)
-            *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = pack8_t<T>(&ov[q8 * 8]);
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 pk;
+            pk.x = pack2<T>(ov[q8 * 8 + 0] * inv_l, ov[q8 * 8 + 1] * inv_l);
+            pk.y = pack2<T>(ov[q8 * 8 + 2] * inv_l, ov[q8 * 8 + 3] * inv_l);
+            pk.z = pack2<T>(ov[q8 * 8 + 4] * inv_l, ov[q8 * 8 + 5] * inv_l);
+            pk.w = pack2<T>(ov[q8 * 8 + 6] * inv_l, ov[q8 * 8 + 7] * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = pk;
+          }
         }
       }
     }
@@ -365,7 +408,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kTcMmaWarp) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, kTcTmemCols);
   }
@@ -378,7 +421,7 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   auto kernel = paged_prefill_tc_kernel<T>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kTcSmemBytes);
   if (e != cudaSuccess) return e;
-  const int tpc = kTcRows / p.group;
+  const int tpc = (kTcTiles * kTcRows) / p.group;
   const int blocks = (max_q_len + tpc - 1) / tpc;
   if (blocks <= 0) return cudaSuccess;
   dim3 grid(blocks, num_kv_heads, num_seqs);
