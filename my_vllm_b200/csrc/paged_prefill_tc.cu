@@ -13,8 +13,10 @@
 //   * warps 0-3 / 4-7: two softmax warpgroups, one per Q tile; thread t of a
 //     group owns row t = TMEM lane t, so row max and row sum need no shuffles.
 //     They stage their Q tile into shared memory (K-major, 128-byte swizzle).
-//   * warp 8: TMA producer streaming 128-token K/V tiles of the paged cache
-//     (8 x 16-token sub-tiles, one lane each) into a 2-stage ring.
+//   * warp 8: TMA producer streaming 128-token K and V tiles of the paged
+//     cache (8 x 16-token sub-tiles, one lane each) into separate rings: K
+//     (3 stages) is released as soon as a tile's S MMAs retire and so runs two
+//     tiles ahead; V (2 stages) is released after the PV MMAs.
 //   * warp 9: allocates all 512 TMEM columns (S_A | O_A | S_B | O_B) and one
 //     thread issues every tcgen05.mma. The order
 //        PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), PV_A(j+1), ...
@@ -52,11 +54,14 @@ constexpr int kTcProducerWarp = 8;
 constexpr int kTcMmaWarp = 9;
 constexpr int kTcHalf = kTcRows * 128;          // [128 rows x 64 elements] = 16 KiB
 constexpr int kTcQ = 0;                         // Q_A, Q_B: 2 x 32 KiB
-constexpr int kTcStage0 = kTcTiles * 2 * kTcHalf;
-constexpr int kTcStageBytes = 4 * kTcHalf;      // K lo/hi + V lo/hi = 64 KiB
-constexpr int kTcStages = 2;
-constexpr int kTcBars = kTcStage0 + kTcStages * kTcStageBytes;
+constexpr int kTcTileBytes = 2 * kTcHalf;       // one K or V tile (lo/hi halves) = 32 KiB
+constexpr int kTcKStages = 3;                   // K is freed after the S MMAs: deeper ring
+constexpr int kTcVStages = 2;                   // V is freed after the PV MMAs
+constexpr int kTcK0 = kTcTiles * kTcTileBytes;
+constexpr int kTcV0 = kTcK0 + kTcKStages * kTcTileBytes;
+constexpr int kTcBars = kTcV0 + kTcVStages * kTcTileBytes;
 constexpr int kTcSmemBytes = 1024 + kTcBars + 256;
+static_assert(kTcSmemBytes <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kTcTmemCols = 512;           // per tile X: S_X at 256X, O_X at 256X+128
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
@@ -74,13 +79,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBars);
-  uint64_t* kv_full = bars + 0;    // [2] TMA -> MMA
-  uint64_t* kv_empty = bars + 2;   // [2] MMA (commit) -> TMA
-  uint64_t* s_full = bars + 4;     // [2] per Q tile: MMA (commit) -> softmax
-  uint64_t* p_ready = bars + 6;    // [2] per Q tile: softmax (128 arrivals) -> MMA
-  uint64_t* o_done = bars + 8;     // [2] per Q tile: MMA (commit) -> epilogue
-  uint64_t* mma_drain = bars + 10; // MMA (commit) -> MMA, before TMEM is freed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_full = bars + 0;     // [3] TMA -> MMA
+  uint64_t* k_empty = bars + 3;    // [3] MMA (commit after the S MMAs) -> TMA
+  uint64_t* v_full = bars + 6;     // [2] TMA -> MMA
+  uint64_t* v_empty = bars + 8;    // [2] MMA (commit after the PV MMAs) -> TMA
+  uint64_t* s_full = bars + 10;    // [2] per Q tile: MMA (commit) -> softmax
+  uint64_t* p_ready = bars + 12;   // [2] per Q tile: softmax (128 arrivals) -> MMA
+  uint64_t* o_done = bars + 14;    // [2] per Q tile: MMA (commit) -> epilogue
+  uint64_t* mma_drain = bars + 16; // MMA (commit) -> MMA, before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,9 +119,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const uint32_t sbase = smem_u32(smem);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcStages; ++i) {
-      mbar_init(smem_u32(&kv_full[i]), 1);
-      mbar_init(smem_u32(&kv_empty[i]), 1);
+    for (int i = 0; i < kTcKStages; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
+    }
+    for (int i = 0; i < kTcVStages; ++i) {
+      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_empty[i]), 1);
     }
     for (int x = 0; x < kTcTiles; ++x) {
       mbar_init(smem_u32(&s_full[x]), 1);
@@ -160,20 +171,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == kTcProducerWarp) {
     // ------------------------------------------------------------ producer --
+    // Issue order K0, K1, then (V_j, K_{j+2}) for j = 0, 1, ...: K runs two
+    // tiles ahead (its stage frees as soon as the S MMAs of a tile retire),
+    // V one to two tiles ahead.
     const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
     const int max_page_idx = (seq_len - 1) / p.block_size;
-    int issued = 0;
-    for (int j = 0; j < n_total; ++j) {
-      const int st = j % kTcStages;
-      if (j >= kTcStages) {
-        const bool got = mbar_wait(smem_u32(&kv_empty[st]), ((j / kTcStages) - 1) & 1);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
+    int issued_k = 0, issued_v = 0;
+    auto load = [&](bool is_v, int j) -> bool {
+      const int nst = is_v ? kTcVStages : kTcKStages;
+      const int st = j % nst;
+      uint64_t* empty = is_v ? v_empty : k_empty;
+      if (j >= nst) {
+        const bool got = mbar_wait(smem_u32(&empty[st]), ((j / nst) - 1) & 1);
+        if (!__all_sync(0xffffffffu, got)) return false;
       }
-      const uint32_t bar = smem_u32(&kv_full[st]);
-      if (lane == 0) mbar_arrive_expect_tx(bar, kTcStageBytes);
+      const uint32_t bar = smem_u32(is_v ? &v_full[st] : &k_full[st]);
+      if (lane == 0) mbar_arrive_expect_tx(bar, kTcTileBytes);
       __syncwarp();
       if (lane < kTcKv / kTileTokens) {
         const int tok = j * kTcKv + lane * kTileTokens;
@@ -186,18 +199,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int page = bt_row[pidx];
         if (page < 0 || page >= p.num_blocks)
           report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
-        const uint32_t dst = sbase + kTcStage0 + st * kTcStageBytes + lane * kHalfTileBytes;
-        tma_load_4d(dst, &tmap_k, bar, 0, kvh, row, page);
-        tma_load_4d(dst + kTcHalf, &tmap_k, bar, 64, kvh, row, page);
-        tma_load_4d(dst + 2 * kTcHalf, &tmap_v, bar, 0, kvh, row, page);
-        tma_load_4d(dst + 3 * kTcHalf, &tmap_v, bar, 64, kvh, row, page);
+        const uint32_t dst =
+            sbase + (is_v ? kTcV0 : kTcK0) + st * kTcTileBytes + lane * kHalfTileBytes;
+        const CUtensorMap* map = is_v ? &tmap_v : &tmap_k;
+        tma_load_4d(dst, map, bar, 0, kvh, row, page);
+        tma_load_4d(dst + kTcHalf, map, bar, 64, kvh, row, page);
       }
-      issued = j + 1;
+      if (is_v) issued_v = j + 1; else issued_k = j + 1;
+      return true;
+    };
+    for (int j = 0; j < min(2, n_total) && ok; ++j) ok = load(false, j);
+    for (int j = 0; j < n_total && ok; ++j) {
+      ok = load(true, j);
+      if (ok && j + 2 < n_total) ok = load(false, j + 2);
     }
     if (!ok) {
       if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
-      for (int j = max(0, issued - kTcStages); j < issued; ++j)
-        mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1);
+      for (int j = max(0, issued_k - kTcKStages); j < issued_k; ++j)
+        mbar_wait(smem_u32(&k_full[j % kTcKStages]), (j / kTcKStages) & 1);
+      for (int j = max(0, issued_v - kTcVStages); j < issued_v; ++j)
+        mbar_wait(smem_u32(&v_full[j % kTcVStages]), (j / kTcVStages) & 1);
     }
   } else if (warp == kTcMmaWarp) {
     // ---------------------------------------------------------- MMA issuer --
@@ -210,7 +231,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       auto issue_s = [&](int x, int j) {
         const uint32_t qbase = sbase + kTcQ + x * 2 * kTcHalf;
-        const uint32_t kbase = sbase + kTcStage0 + (j % kTcStages) * kTcStageBytes;
+        const uint32_t kbase = sbase + kTcK0 + (j % kTcKStages) * kTcTileBytes;
 #pragma unroll
         for (int k = 0; k < kHeadDim / 16; ++k)
           umma_f16(tmem_base + x * 256, kmajor(qbase, k), kmajor(kbase, k), idesc_s,
@@ -218,8 +239,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         umma_commit(smem_u32(&s_full[x]));
       };
       auto issue_pv = [&](int x, int j) {
-        const uint32_t vbase =
-            sbase + kTcStage0 + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf;
+        const uint32_t vbase = sbase + kTcV0 + (j % kTcVStages) * kTcTileBytes;
         const uint32_t tP = tmem_base + x * 256;  // P (16-bit, packed) over S
 #pragma unroll
         for (int k = 0; k < kTcKv / 16; ++k)
@@ -227,12 +247,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                       smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
                       (j > 0 || k > 0) ? 1u : 0u);
       };
-      int kv_ready = -1;  // highest tile whose kv_full phase was observed
-      auto wait_kv = [&](int j) {
-        if (j <= kv_ready) return true;
-        if (!mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1)) return false;
+      int k_ready = -1, v_ready = -1;  // highest tiles whose full phase was observed
+      auto wait_k = [&](int j) {
+        if (j <= k_ready) return true;
+        if (!mbar_wait(smem_u32(&k_full[j % kTcKStages]), (j / kTcKStages) & 1)) return false;
         tc_fence_after_sync();
-        kv_ready = j;
+        k_ready = j;
+        return true;
+      };
+      auto wait_v = [&](int j) {
+        if (j <= v_ready) return true;
+        if (!mbar_wait(smem_u32(&v_full[j % kTcVStages]), (j / kTcVStages) & 1)) return false;
+        tc_fence_after_sync();
+        v_ready = j;
         return true;
       };
       // One Q tile's step j: PV of tile j, then S of tile j + 1.
@@ -240,24 +267,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (j >= n_x) return true;
         if (!mbar_wait(smem_u32(&p_ready[x]), j & 1)) return false;
         tc_fence_after_sync();
+        if (!wait_v(j)) return false;
         issue_pv(x, j);
         if (j == n_x - 1) umma_commit(smem_u32(&o_done[x]));
         if (j + 1 < n_x) {
-          if (!wait_kv(j + 1)) return false;
+          if (!wait_k(j + 1)) return false;
           issue_s(x, j + 1);
         }
         return true;
       };
       // prologue: S of tile 0 for both Q tiles
-      if (!wait_kv(0)) ok = false;
+      if (!wait_k(0)) ok = false;
       if (ok && n_a > 0) issue_s(0, 0);
       if (ok && n_b > 0) issue_s(1, 0);
+      if (ok) umma_commit(smem_u32(&k_empty[0]));  // after every S of tile 0
       for (int j = 0; j < n_total && ok; ++j) {
         if (!step(0, n_a, j) || !step(1, n_b, j)) {
           ok = false;
           break;
         }
-        umma_commit(smem_u32(&kv_empty[j % kTcStages]));  // after every reader of tile j
+        umma_commit(smem_u32(&v_empty[j % kTcVStages]));  // after every PV of tile j
+        if (j + 1 < n_total)
+          umma_commit(smem_u32(&k_empty[(j + 1) % kTcKStages]));  // every S of tile j+1
       }
       if (!ok) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
       // every MMA this thread issued has completed before TMEM is released
@@ -355,14 +386,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Last KV tile: V rows past the sequence end may hold never-written
         // cache slots (possibly NaN) and P = 0 does not cancel NaN. Both
         // warpgroups write the same zeros, each before its own PV.
-        const bool landed = mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1);
+        const bool landed = mbar_wait(smem_u32(&v_full[j % kTcVStages]), (j / kTcVStages) & 1);
         if (!__all_sync(0xffffffffu, landed)) {
           ok = false;
           break;
         }
         if (kbase + t >= seq_len) {
-          uint8_t* vrow =
-              smem + kTcStage0 + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf + t * 128;
+          uint8_t* vrow = smem + kTcV0 + (j % kTcVStages) * kTcTileBytes + t * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
