@@ -211,22 +211,4 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for x <= 8 (softmax exponents): range reduction
-// 2^x = 2^floor(x) * 2^f, f in [0, 1), with 2^f from a cubic
-// 1 + f (c1 + f (c2 + f c3)) whose coefficients were fitted (least squares on
-// relative error, p(0) = 1 and p(1) = 2 imposed) for this project; max
-// relative error 1.1e-4, well inside the 2^-8 spacing of the 16-bit P it
-// feeds. Inputs below -126 return 0. Used for part of each softmax row so the
-// MUFU pipe and the FMA pipe share the exponentials.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -127.0f);
-  const float j = floorf(x);
-  const float f = x - j;
-  float p = fmaf(f, 0.0782528954f, 0.2262933417f);
-  p = fmaf(f, p, 0.6954537629f);
-  p = fmaf(f, p, 1.0f);
-  const int bits = __float_as_int(p) + (static_cast<int>(j) << 23);
-  return x <= -127.0f ? 0.0f : __int_as_float(bits);
-}
-
 }  // namespace b200
