@@ -224,40 +224,26 @@ int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv
                   "forced split leaves partitions longer than 8192 tokens");
     if (parts > tiles) parts = tiles;
   } else {
-    // Fill the machine: CTAs = seqs x KV heads x parts. Pick the smallest
-    // split whose last wave is >= 90% full (or that leaves >= 2 waves of
-    // equal work when the batch alone already fills the SMs).
+    // The kernel is HBM-bound: it needs bytes in flight, not full waves of
+    // CTAs, and every extra partition costs a pipeline ramp plus partial
+    // outputs. So split only (a) to give every SM at least one CTA, and (b)
+    // for ragged batches, so no CTA holds more than 1/12 of the average
+    // per-SM work (the longest sequences would otherwise finish last on a few
+    // SMs; 1/12 measured best on a 124-sequence batch of U[128, 8192]).
     const int64_t units = (int64_t)num_seqs * num_kv_heads;
-    const int64_t slots = (int64_t)sm_count() * b200::decode_ctas_per_sm();
+    const int64_t sms = sm_count();
     parts = min_parts;
-    // Ragged batches: no CTA should hold more than a quarter of the average
-    // per-slot work, or the longest sequences finish last on a few SMs.
+    if (units * parts < sms) parts = (sms + units - 1) / units;
     const int64_t max_tokens = (int64_t)num_seqs * max_kv_len;
     const int64_t total = (total_kv_tokens > 0 && total_kv_tokens < max_tokens)
                               ? total_kv_tokens : max_tokens;
     if (total < max_tokens) {
       const int64_t total_tiles = (total + b200::kTileTokens - 1) / b200::kTileTokens;
-      const double per_slot = double(total_tiles) * num_kv_heads / double(slots);
-      int64_t balance = (int64_t)(4.0 * double(tiles) / per_slot + 0.999999);
+      const double per_sm = double(total_tiles) * num_kv_heads / double(sms);
+      int64_t balance = (int64_t)(12.0 * double(tiles) / per_sm + 0.999999);
       const int64_t cap = tiles / 4 > 1 ? tiles / 4 : 1;  // >= 4 tiles per partition
       if (balance > cap) balance = cap;
       if (balance > parts) parts = balance;
-    }
-    if (units * parts < 2 * slots) {
-      int64_t best = parts;
-      double best_eff = 0.0;
-      for (int64_t pp = min_parts; pp <= 64; ++pp) {
-        const int64_t part_tiles = (tiles + pp - 1) / pp;
-        if (part_tiles < 4 && pp > min_parts) break;
-        const double waves = double(units * pp) / double(slots);
-        const double eff = waves / double((int64_t)(waves + 0.999999));
-        if (eff > best_eff + 1e-9 || (waves >= 2.0 && eff >= 0.9)) {
-          best = pp;
-          best_eff = eff;
-        }
-        if (waves >= 2.0 && eff >= 0.9) break;
-      }
-      parts = best;
     }
   }
   const int64_t part_tiles = (tiles + parts - 1) / parts;
