@@ -334,18 +334,66 @@ def run_ours(args, rank, world, local_rank):
     backend.check_status()
 
     # ---- end to end through the public API with host buffers ----
-    # Every step copies its inputs host->device from pinned memory and reads its
-    # output back to the host. As in a serving loop, the copies of neighbouring
-    # steps overlap this step's kernels: two copy streams, double-buffered
-    # device staging, events between them; the timed region ends only after the
-    # last step's output has landed on the host.
-    names = ("q", "key", "value", "slot_mapping", "block_tables", "seq_lens",
-             "query_start_loc")
-    host = {name: getattr(w, name).cpu().pin_memory() for name in names}
-    dev = [{name: torch.empty_like(getattr(w, name)) for name in names} for _ in range(2)]
+    # The engine runs a pure-decode step as a full-decode CUDA Graph
+    # (ModelRunner.run_model -> build_plan -> plan_full_decode_graph -> replay,
+    # model_runner.py:496-518 and 676-766). Each step here: one packed
+    # host->device copy of that step's inputs from pinned memory, build_plan,
+    # plan_full_decode_graph, a replay of the captured append + attention, and a
+    # device->host copy of the output. Two staging slots let the copies of
+    # neighbouring steps overlap this step's kernels on two copy streams; the
+    # timed region ends only after the last output has landed on the host.
+    layout = [("q", w.q), ("key", w.key), ("value", w.value), ("slot_mapping", w.slot_mapping),
+              ("block_tables", w.block_tables), ("seq_lens", w.seq_lens),
+              ("query_start_loc", w.query_start_loc)]
+    offsets, total = {}, 0
+    for name, t in layout:
+        offsets[name] = total
+        total += (t.numel() * t.element_size() + 255) // 256 * 256
+
+    def views(buf):
+        out = {}
+        for name, t in layout:
+            n = t.numel() * t.element_size()
+            out[name] = buf[offsets[name]: offsets[name] + n].view(t.dtype).view(t.shape)
+        return out
+
+    host_packed = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    for name, t in layout:
+        views(host_packed)[name].copy_(t)
+    staging = [torch.empty(total, dtype=torch.uint8, device=device) for _ in range(2)]
+    sv = [views(buf) for buf in staging]
+    for b in range(2):
+        staging[b].copy_(host_packed)
+    commons = [type(common)(**{**common.__dict__, "query_start_loc": sv[b]["query_start_loc"],
+                               "seq_lens": sv[b]["seq_lens"], "slot_mapping": sv[b]["slot_mapping"],
+                               "block_tables": sv[b]["block_tables"]}) for b in range(2)]
+    width = w.block_tables.size(1)
+    states = [backend.create_full_decode_graph_state(w.num_seqs, w.num_seqs * width, device)
+              for _ in range(2)]
     out_dev = [torch.empty_like(w.q) for _ in range(2)]
     out_host = [torch.empty(w.q.shape, dtype=w.q.dtype, pin_memory=True) for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    graphs = []
+    for b in range(2):
+        plan_b = backend.build_plan(commons[b])
+        backend.plan_full_decode_graph(states[b], plan_b)
+        backend.activate_full_decode_graph(states[b])
+        try:
+            def body(b=b, plan_b=plan_b):
+                d = sv[b]
+                ops.store_kvcache(d["key"], d["value"], w.k_cache, w.v_cache, d["slot_mapping"])
+                o = backend.forward(d["q"], d["key"], d["value"], w.k_cache, w.v_cache, plan_b)
+                out_dev[b].copy_(o)
+
+            body()
+            torch.cuda.synchronize(device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                body()
+            graphs.append(graph)
+        finally:
+            backend.deactivate_full_decode_graph()
+    torch.cuda.synchronize(device)
+    h2d = total
     d2h = out_host[0].numel() * out_host[0].element_size()
     h2d_stream = torch.cuda.Stream(device)
     d2h_stream = torch.cuda.Stream(device)
@@ -357,19 +405,13 @@ def run_ours(args, rank, world, local_rank):
         b = i % 2
         h2d_stream.wait_event(compute_done[b])  # slot b's previous step has consumed it
         with torch.cuda.stream(h2d_stream):
-            for name in names:
-                dev[b][name].copy_(host[name], non_blocking=True)
+            staging[b].copy_(host_packed, non_blocking=True)
             h2d_done[b].record(h2d_stream)
         stream.wait_event(h2d_done[b])
         stream.wait_event(d2h_done[b])
-        d = dev[b]
-        common_e2e = type(common)(**{**common.__dict__, "query_start_loc": d["query_start_loc"],
-                                     "seq_lens": d["seq_lens"], "slot_mapping": d["slot_mapping"],
-                                     "block_tables": d["block_tables"]})
-        p = backend.build_plan(common_e2e)
-        ops.store_kvcache(d["key"], d["value"], w.k_cache, w.v_cache, d["slot_mapping"])
-        out = backend.forward(d["q"], d["key"], d["value"], w.k_cache, w.v_cache, p)
-        out_dev[b].copy_(out, non_blocking=True)
+        step_plan = backend.build_plan(commons[b])
+        backend.plan_full_decode_graph(states[b], step_plan)
+        graphs[b].replay()
         compute_done[b].record(stream)
         d2h_stream.wait_event(compute_done[b])
         with torch.cuda.stream(d2h_stream):
@@ -402,6 +444,8 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_leg(args.cpu_sample_seqs)
 
+    graphs.clear()  # release the captured graphs before tearing the process group down
+    torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank != 0:
@@ -456,8 +500,10 @@ def run_ours(args, rank, world, local_rank):
             "ms_per_step": round(e2e_ms, 5),
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": "B200PagedBackend.build_plan/forward + ops.store_kvcache, pinned host "
-                   "buffers, H2D/D2H of neighbouring steps overlapped on two copy streams",
+            "api": "engine full-decode CUDA Graph step: packed H2D from pinned memory, "
+                   "B200PagedBackend.build_plan + plan_full_decode_graph, graph replay of "
+                   "ops.store_kvcache + B200PagedBackend.forward, D2H of the output; copies of "
+                   "neighbouring steps overlapped on two copy streams",
         },
         "gpu_launches": launches_per_step * args.steps,
     }

@@ -7,6 +7,7 @@ is no CPU path: a CPU tensor or a missing library raises.
 
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 
 import torch
@@ -86,8 +87,60 @@ def store_kvcache(
     _native.check(rc, "b200_store_kvcache")
 
 
+def build_slot_mapping(
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    block_size: int,
+    num_tokens: int,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Cache slots of the new tokens, computed on the GPU from the batch
+    metadata (the host loop of ModelRunner.prepare_model_input,
+    nanovllm/engine/model_runner.py:414-425). Returns int32 [num_tokens]."""
+    for name, t in (("block_tables", block_tables), ("seq_lens", seq_lens),
+                    ("query_start_loc", query_start_loc)):
+        _require_cuda(name, t)
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    num_seqs = seq_lens.numel()
+    if query_start_loc.numel() != num_seqs + 1 or block_tables.size(0) != num_seqs:
+        raise ValueError("metadata lengths do not match num_seqs")
+    if out is None:
+        out = torch.empty(num_tokens, dtype=torch.int32, device=seq_lens.device)
+    elif out.dtype != torch.int32 or out.numel() != num_tokens or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 tensor of num_tokens entries")
+    rc = _native.load_library().b200_build_slot_mapping(
+        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(),
+        query_start_loc.data_ptr(), num_seqs, int(num_tokens), int(block_size),
+        out.data_ptr(), _stream_handle(seq_lens.device),
+    )
+    _native.check(rc, "b200_build_slot_mapping")
+    return out
+
+
 def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.PagedCache:
-    """Describe a pair of NHD caches ``[num_blocks, block_size, Hkv, D]``."""
+    """Describe a pair of NHD caches ``[num_blocks, block_size, Hkv, D]``.
+
+    Descriptors are cached by (pointers, shape, strides, dtype): layers reuse
+    the same cache views every step, so the checks run once per view."""
+    key = (k_cache.data_ptr(), v_cache.data_ptr(), tuple(k_cache.shape), tuple(v_cache.shape),
+           k_cache.stride(), v_cache.stride(), k_cache.dtype, v_cache.dtype)
+    desc = _CACHE_DESCS.get(key)
+    if desc is None:
+        desc = _make_cache_desc(k_cache, v_cache)
+        if len(_CACHE_DESCS) > 4096:
+            _CACHE_DESCS.clear()
+        _CACHE_DESCS[key] = desc
+    return desc
+
+
+_CACHE_DESCS: dict = {}
+
+
+def _make_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.PagedCache:
     if k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
         raise ValueError(
             "key and value caches must have shape [pages, block_size, num_kv_heads, head_dim]"
@@ -114,7 +167,12 @@ class DecodePlan:
     workspace_bytes: int
 
     def as_native(self) -> _native.DecodePlan:
-        return _native.DecodePlan(self.num_parts, self.part_tokens, self.workspace_bytes)
+        return _native_plan(self.num_parts, self.part_tokens, self.workspace_bytes)
+
+
+@functools.lru_cache(maxsize=256)
+def _native_plan(num_parts: int, part_tokens: int, workspace_bytes: int) -> _native.DecodePlan:
+    return _native.DecodePlan(num_parts, part_tokens, workspace_bytes)
 
 
 def plan_decode(
