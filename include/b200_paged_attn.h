@@ -83,6 +83,21 @@ B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
                        int32_t* status, void* stream);
 
 /*
+ * Slot mapping of the new tokens, built on the device. Replaces the host loop
+ * of ModelRunner.prepare_model_input (nanovllm/engine/model_runner.py:414-425).
+ * Token t of sequence s (rows [query_start_loc[s], query_start_loc[s+1]))
+ * sits at KV position seq_lens[s] - q_len + (t - query_start_loc[s]) and is
+ * stored in slot block_tables[s][pos / block_size] * block_size
+ * + pos % block_size; a block-table entry of -1 (no cache) gives slot -1.
+ * block_tables rows must hold ceil(seq_lens[s] / block_size) entries.
+ * slot_mapping: int32 [num_tokens] output.
+ */
+B200_API int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride,
+                                     const int32_t* seq_lens, const int32_t* query_start_loc,
+                                     int32_t num_seqs, int32_t num_tokens, int32_t block_size,
+                                     int32_t* slot_mapping, void* stream);
+
+/*
  * Paged KV cache description (NHD). Strides are in elements; the innermost
  * (head_dim) stride is 1. Every stride must be a multiple of 8 elements and
  * both base pointers 16-byte aligned (TMA rules).

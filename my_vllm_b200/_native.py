@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "b200_abi_version",
     "b200_last_error",
     "b200_store_kvcache",
+    "b200_build_slot_mapping",
     "b200_paged_decode_plan",
     "b200_paged_decode",
     "b200_paged_prefill",
@@ -85,6 +86,7 @@ _SIGNATURES = {
         [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _I32, _I64, _I64, _I32, _I64, _VP, _VP],
         _I32,
     ),
+    "b200_build_slot_mapping": ([_VP, _I64, _VP, _VP, _I32, _I32, _I32, _VP, _VP], _I32),
     "b200_paged_decode_plan": (
         [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32, ctypes.POINTER(DecodePlan)],
         _I32,

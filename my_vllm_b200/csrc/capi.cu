@@ -200,6 +200,25 @@ int b200_store_kvcache(const void* key, int64_t key_row_stride, const void* valu
   return B200_OK;
 }
 
+int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride,
+                            const int32_t* seq_lens, const int32_t* query_start_loc,
+                            int32_t num_seqs, int32_t num_tokens, int32_t block_size,
+                            int32_t* slot_mapping, void* stream) {
+  g_last_error.clear();
+  if (num_seqs < 0 || num_tokens < 0 || block_size <= 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be non-negative, block_size positive");
+  if (num_tokens == 0) return B200_OK;
+  if (num_seqs == 0) return fail(B200_ERR_INVALID_ARGUMENT, "tokens without sequences");
+  if (!block_tables || !seq_lens || !query_start_loc || !slot_mapping)
+    return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  cudaError_t e = b200::launch_build_slot_mapping(block_tables, block_table_stride, seq_lens,
+                                                  query_start_loc, num_seqs, num_tokens,
+                                                  block_size, slot_mapping,
+                                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "slot mapping launch");
+  return B200_OK;
+}
+
 int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t head_dim, int32_t block_size, int32_t max_kv_len,
                            int64_t total_kv_tokens, int32_t force_num_parts,

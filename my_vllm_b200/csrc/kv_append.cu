@@ -130,4 +130,43 @@ cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
                        slot64, num_tokens, row_bytes, num_slots, status, stream);
 }
 
+// Slot of every new token, from the batch metadata (see b200_build_slot_mapping).
+__global__ void __launch_bounds__(256)
+    build_slot_mapping_kernel(const int32_t* __restrict__ block_tables, int64_t bt_stride,
+                              const int32_t* __restrict__ seq_lens,
+                              const int32_t* __restrict__ query_start_loc, int num_seqs,
+                              int num_tokens, int block_size, int32_t* __restrict__ slots) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= num_tokens) return;
+  // sequence s with query_start_loc[s] <= t < query_start_loc[s + 1]
+  int lo = 0, hi = num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(query_start_loc + mid) <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  const int s = lo;
+  const int q0 = __ldg(query_start_loc + s);
+  const int q_len = __ldg(query_start_loc + s + 1) - q0;
+  const int pos = __ldg(seq_lens + s) - q_len + (t - q0);
+  int32_t slot = -1;
+  if (pos >= 0) {
+    const int32_t page = __ldg(block_tables + (int64_t)s * bt_stride + pos / block_size);
+    if (page >= 0) slot = page * block_size + pos % block_size;
+  }
+  slots[t] = slot;
+}
+
+cudaError_t launch_build_slot_mapping(const int32_t* block_tables, int64_t bt_stride,
+                                      const int32_t* seq_lens, const int32_t* query_start_loc,
+                                      int num_seqs, int num_tokens, int block_size,
+                                      int32_t* slots, cudaStream_t stream) {
+  const int threads = 256;
+  const int blocks = (num_tokens + threads - 1) / threads;
+  build_slot_mapping_kernel<<<blocks, threads, 0, stream>>>(
+      block_tables, bt_stride, seq_lens, query_start_loc, num_seqs, num_tokens, block_size,
+      slots);
+  return cudaGetLastError();
+}
+
 }  // namespace b200

@@ -57,4 +57,9 @@ cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
                              int64_t row_elems, int32_t elem_bytes, int64_t num_slots,
                              int32_t* status, cudaStream_t stream);
 
+cudaError_t launch_build_slot_mapping(const int32_t* block_tables, int64_t bt_stride,
+                                      const int32_t* seq_lens, const int32_t* query_start_loc,
+                                      int num_seqs, int num_tokens, int block_size,
+                                      int32_t* slots, cudaStream_t stream);
+
 }  // namespace b200

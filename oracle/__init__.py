@@ -14,3 +14,4 @@ from .paged_attention import (  # noqa: F401
     paged_attention_from_tables,
     to_f32,
 )
+from .metadata import slot_mapping  # noqa: F401,E402

@@ -127,3 +127,30 @@ def test_unaligned_rows_use_narrow_vectors(cuda_device):
     torch.cuda.synchronize()
     assert np.array_equal(storage(k_cache), k_ref)
     assert np.array_equal(storage(v_cache), v_ref)
+
+
+def test_device_slot_mapping_known_answers(cuda_device):
+    # the reference's metadata known answers (test_model_runner_metadata.py:138-241)
+    bt = torch.tensor([[7, 4], [9, -1]], dtype=torch.int32, device=cuda_device)
+    slots = ops.build_slot_mapping(
+        bt, torch.tensor([19, 5], dtype=torch.int32, device=cuda_device),
+        torch.tensor([0, 3, 8], dtype=torch.int32, device=cuda_device), 16, 8)
+    assert slots.tolist() == [64, 65, 66, 144, 145, 146, 147, 148]
+    bt = torch.tensor([[2, -1], [4, 5]], dtype=torch.int32, device=cuda_device)
+    slots = ops.build_slot_mapping(
+        bt, torch.tensor([3, 18], dtype=torch.int32, device=cuda_device),
+        torch.tensor([0, 3, 4], dtype=torch.int32, device=cuda_device), 16, 4)
+    assert slots.tolist() == [32, 33, 34, 81]
+
+
+def test_device_slot_mapping_matches_oracle_on_config3(cuda_device):
+    w = workloads.config3(device=cuda_device)
+    qsl = w.extra["qsl_host"]
+    lens = w.extra["seq_lens_host"]
+    tables = [row[: c].tolist() for row, c in zip(w.block_tables.cpu(), w.block_counts)]
+    cached = [lens[i] - (qsl[i + 1] - qsl[i]) for i in range(len(lens))]
+    expected = oracle.slot_mapping(tables, cached, lens, w.block_size)
+    got = ops.build_slot_mapping(w.block_tables, w.seq_lens, w.query_start_loc, w.block_size,
+                                 w.num_tokens)
+    assert got.tolist() == expected
+    assert expected == w.extra["slots_host"][: w.num_tokens]

@@ -90,3 +90,12 @@ def test_config1_append_and_decode_match_reference():
         storage(w.q), k_cache, v_cache, w.block_tables.numpy(), w.seq_lens.numpy(),
         w.query_start_loc.numpy(), w.block_size, out_dtype="float32")
     np.testing.assert_allclose(out32, g["out_f32"], atol=2e-5, rtol=1e-4)
+
+
+def test_slot_mapping_known_answers():
+    # tests/test_model_runner_metadata.py:138-187 (prefix extension + fresh
+    # prefill) and :219-241 (prefill + decode) of the reference
+    assert oracle.slot_mapping([[7, 4], [9]], [16, 0], [19, 5], 16) == [
+        64, 65, 66, 144, 145, 146, 147, 148]
+    assert oracle.slot_mapping([[2], [4, 5]], [0, 17], [3, 18], 16) == [32, 33, 34, 81]
+    assert oracle.slot_mapping([[], []], [0, 0], [4, 2], 16) == [-1] * 6
