@@ -48,6 +48,7 @@ extern "C" {
 #define B200_STATUS_WAIT_TIMEOUT 0x4
 #define B200_STATUS_TMEM_ALLOC_FAILED 0x8
 #define B200_STATUS_PLAN_EXCEEDED 0x10 /* a sequence is longer than the decode plan covers */
+#define B200_STATUS_POSITION_OUT_OF_RANGE 0x20 /* a RoPE position beyond the cos/sin table */
 
 /* element types of Q / K / V / O */
 #define B200_DTYPE_FLOAT16 0
@@ -81,6 +82,31 @@ B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
                        int64_t num_tokens, int64_t row_elems,
                        int32_t elem_bytes, int64_t num_slots,
                        int32_t* status, void* stream);
+
+/*
+ * Fused q/k RMSNorm + rotary embedding + KV append: the step before attention
+ * of Qwen3Attention.forward (nanovllm/models/qwen3.py:96-100: q_norm, k_norm
+ * from layers/layernorm.py:30-41, the neox rotary embedding of
+ * layers/rotary_embedding.py:7-15,40-51) fused with the KV append of
+ * Attention.forward (layers/attention.py:139-141). For every token t:
+ *   q_out[t, h] = rope(rmsnorm(q[t, h]) * q_weight, positions[t])   (all q heads)
+ *   k_cache[slot_mapping[t], h] = rope(rmsnorm(k[t, h]) * k_weight, positions[t])
+ *   v_cache[slot_mapping[t], h] = v[t, h]
+ * RMSNorm is x / sqrt(mean(x^2) + eps) in fp32 rounded to the element type,
+ * times the element-type weight and rounded; rope rotates pairs (i, i + 64)
+ * in fp32 with cos = cos_sin_cache[pos][i], sin = cos_sin_cache[pos][64 + i]
+ * and rounds. Slots of -1 skip the cache writes (q is still produced).
+ * head_dim must be 128; q/k/v rows may be strided views of the fused qkv
+ * projection (heads packed within a row); q_out may alias q.
+ */
+B200_API int b200_qk_norm_rope_append(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+    int64_t k_token_stride, const void* v, int64_t v_token_stride, void* q_out,
+    int64_t q_out_token_stride, int64_t q_out_head_stride, const void* q_weight,
+    const void* k_weight, float eps, const int64_t* positions, const float* cos_sin_cache,
+    int64_t max_position, void* k_cache, void* v_cache, int64_t cache_slot_stride,
+    const int32_t* slot_mapping, int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype, int64_t num_slots, int32_t* status, void* stream);
 
 /*
  * Slot mapping of the new tokens, built on the device. Replaces the host loop

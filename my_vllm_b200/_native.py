@@ -23,6 +23,7 @@ STATUS_PAGE_OUT_OF_RANGE = 0x2
 STATUS_WAIT_TIMEOUT = 0x4
 STATUS_TMEM_ALLOC_FAILED = 0x8
 STATUS_PLAN_EXCEEDED = 0x10
+STATUS_POSITION_OUT_OF_RANGE = 0x20
 
 DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
@@ -37,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "b200_last_error",
     "b200_store_kvcache",
     "b200_build_slot_mapping",
+    "b200_qk_norm_rope_append",
     "b200_paged_decode_plan",
     "b200_paged_decode",
     "b200_paged_prefill",
@@ -87,6 +89,13 @@ _SIGNATURES = {
         _I32,
     ),
     "b200_build_slot_mapping": ([_VP, _I64, _VP, _VP, _I32, _I32, _I32, _VP, _VP], _I32),
+    "b200_qk_norm_rope_append": (
+        [
+            _VP, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _F32, _VP, _VP,
+            _I64, _VP, _VP, _I64, _VP, _I64, _I32, _I32, _I32, _I32, _I64, _VP, _VP,
+        ],
+        _I32,
+    ),
     "b200_paged_decode_plan": (
         [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32, ctypes.POINTER(DecodePlan)],
         _I32,
@@ -167,6 +176,7 @@ def describe_status(bits: int) -> str:
         (STATUS_WAIT_TIMEOUT, "pipeline wait timed out"),
         (STATUS_TMEM_ALLOC_FAILED, "tensor-memory allocation failed"),
         (STATUS_PLAN_EXCEEDED, "sequence longer than the decode plan"),
+        (STATUS_POSITION_OUT_OF_RANGE, "rotary position beyond the cos/sin table"),
     ):
         if bits & bit:
             names.append(name)

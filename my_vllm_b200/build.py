@@ -21,6 +21,7 @@ LIBRARY_PATH = PACKAGE_DIR / LIBRARY_NAME
 
 SOURCES = (
     "kv_append.cu",
+    "rope_append.cu",
     "paged_decode.cu",
     "paged_prefill_tc.cu",
     "capi.cu",

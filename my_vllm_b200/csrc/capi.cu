@@ -17,6 +17,7 @@
 #include "../../include/b200_paged_attn.h"
 #include "paged_decode.cuh"
 #include "paged_prefill.cuh"
+#include "rope_append.cuh"
 
 namespace {
 
@@ -197,6 +198,68 @@ int b200_store_kvcache(const void* key, int64_t key_row_stride, const void* valu
       slot_mapping, slot_is_int64 != 0, num_tokens, row_elems, elem_bytes, num_slots, status,
       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
+  return B200_OK;
+}
+
+int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head_stride,
+                             const void* k, int64_t k_token_stride, const void* v,
+                             int64_t v_token_stride, void* q_out, int64_t q_out_token_stride,
+                             int64_t q_out_head_stride, const void* q_weight,
+                             const void* k_weight, float eps, const int64_t* positions,
+                             const float* cos_sin_cache, int64_t max_position, void* k_cache,
+                             void* v_cache, int64_t cache_slot_stride,
+                             const int32_t* slot_mapping, int64_t num_tokens,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t dtype, int64_t num_slots, int32_t* status, void* stream) {
+  g_last_error.clear();
+  if (head_dim != b200::kRopeHeadDim) return fail(B200_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (dtype != B200_DTYPE_BFLOAT16 && dtype != B200_DTYPE_FLOAT16)
+    return fail(B200_ERR_UNSUPPORTED, "dtype must be float16 or bfloat16");
+  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_position <= 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  if (num_tokens == 0) return B200_OK;
+  if (!q || !k || !v || !q_out || !q_weight || !k_weight || !positions || !cos_sin_cache ||
+      !k_cache || !v_cache || !slot_mapping)
+    return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+        reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(k_cache)) & 3) ||
+      ((reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(v_cache)) & 15) ||
+      (q_token_stride | q_head_stride | k_token_stride | q_out_token_stride |
+       q_out_head_stride) & 1 ||
+      (v_token_stride | cache_slot_stride) & 7)
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "q/k/q_out/k_cache must be 4-byte aligned with even strides; v and v_cache "
+                "16-byte aligned with strides that are multiples of 8");
+  if (cache_slot_stride < (int64_t)num_kv_heads * head_dim)
+    return fail(B200_ERR_INVALID_ARGUMENT, "cache slot stride must cover all KV heads");
+  b200::RopeAppendParams p;
+  p.q = q;
+  p.q_token_stride = q_token_stride;
+  p.q_head_stride = q_head_stride;
+  p.k = k;
+  p.k_token_stride = k_token_stride;
+  p.v = v;
+  p.v_token_stride = v_token_stride;
+  p.q_out = q_out;
+  p.q_out_token_stride = q_out_token_stride;
+  p.q_out_head_stride = q_out_head_stride;
+  p.q_weight = q_weight;
+  p.k_weight = k_weight;
+  p.eps = eps;
+  p.positions = positions;
+  p.cos_sin_cache = cos_sin_cache;
+  p.max_position = max_position;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.cache_slot_stride = cache_slot_stride;
+  p.slot_mapping = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.num_slots = num_slots;
+  p.status = status;
+  cudaError_t e = b200::launch_qk_norm_rope_append(p, dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "q/k norm + rope + append launch");
   return B200_OK;
 }
 

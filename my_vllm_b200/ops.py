@@ -87,6 +87,77 @@ def store_kvcache(
     _native.check(rc, "b200_store_kvcache")
 
 
+def qk_norm_rope_append(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    positions: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    eps: float,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    q_out: torch.Tensor | None = None,
+    *,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Fused q/k RMSNorm + neox rotary embedding + KV append (one kernel).
+
+    Replaces ``q_norm``, ``k_norm`` and ``rotary_emb`` of
+    Qwen3Attention.forward (nanovllm/models/qwen3.py:96-100) plus the KV
+    append of Attention.forward (attention.py:139-141): returns the rotated q
+    (into ``q_out``, which may be ``q`` itself) and writes the rotated k and
+    the v rows into their cache slots. ``cos_sin_cache`` is the engine's
+    fp32 table ([max_position, 128] or [max_position, 1, 128]: cos | sin).
+    """
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    for name, t in (("q", q), ("k", k), ("v", v), ("positions", positions),
+                    ("q_weight", q_weight), ("k_weight", k_weight),
+                    ("cos_sin_cache", cos_sin_cache), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t)
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k and v must share one float16/bfloat16 dtype")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("caches must have the q dtype")
+    if q_weight.dtype != q.dtype or k_weight.dtype != q.dtype:
+        raise TypeError("norm weights must have the q dtype")
+    if positions.dtype != torch.int64 or slot_mapping.dtype != torch.int32:
+        raise TypeError("positions must be int64 and slot_mapping int32")
+    if cos_sin_cache.dtype != torch.float32 or not cos_sin_cache.is_contiguous():
+        raise TypeError("cos_sin_cache must be a contiguous float32 tensor")
+    if k.shape != v.shape or k.shape[0] != T or k.shape[2] != D:
+        raise ValueError("k and v must be [tokens, num_kv_heads, head_dim]")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} rows must be contiguous in head_dim")
+    if k.stride(1) != D or v.stride(1) != D:
+        raise ValueError("k/v heads must be packed (stride(1) == head_dim)")
+    if k_cache.stride(1) != Hkv * D or k_cache.stride() != v_cache.stride():
+        raise ValueError("cache slots must be packed [num_blocks, block_size, Hkv, head_dim]")
+    if slot_mapping.numel() != T or positions.numel() != T:
+        raise ValueError("one slot and one position per token")
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    if q_out.shape != q.shape or q_out.dtype != q.dtype or q_out.stride(-1) != 1:
+        raise ValueError("q_out must match q")
+    max_position = cos_sin_cache.numel() // D
+    num_slots = k_cache.size(0) * k_cache.size(1)
+    rc = _native.load_library().b200_qk_norm_rope_append(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), v.data_ptr(),
+        v.stride(0), q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_weight.data_ptr(),
+        k_weight.data_ptr(), float(eps), positions.data_ptr(), cos_sin_cache.data_ptr(),
+        max_position, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(1),
+        slot_mapping.data_ptr(), T, Hq, Hkv, D, _DTYPES[q.dtype], num_slots, _ptr(status),
+        _stream_handle(q.device),
+    )
+    _native.check(rc, "b200_qk_norm_rope_append")
+    return q_out
+
+
 def build_slot_mapping(
     block_tables: torch.Tensor,
     seq_lens: torch.Tensor,

@@ -15,3 +15,4 @@ from .paged_attention import (  # noqa: F401
     to_f32,
 )
 from .metadata import slot_mapping  # noqa: F401,E402
+from .rope import cos_sin_cache, rms_norm, rope_neox  # noqa: F401,E402

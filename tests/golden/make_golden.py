@@ -178,6 +178,57 @@ def config1_case(reference_fn, KVCacheStore, CustomOpConfig):
                 cache_digest=digest(w.k_cache, w.v_cache))
 
 
+def rope_inputs(seed=2027):
+    """Seeded q/k/v rows of a fused qkv projection (Qwen3 head layout), norm
+    weights near 1, positions below 4096, rope theta 1e6 (Qwen3)."""
+    g = torch.Generator().manual_seed(seed)
+    T, Hq, Hkv, D = 9, 4, 2, 128
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    positions = torch.randint(0, 4096, (T,), generator=g)
+    q_weight = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    k_weight = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    return dict(qkv=qkv, positions=positions, q_weight=q_weight, k_weight=k_weight, T=T, Hq=Hq,
+                Hkv=Hkv, D=D, eps=1e-6, max_position=4096, base=1e6)
+
+
+def rope_cos_sin_cache(head_dim, max_position, base):
+    """The engine's table, computed the way RotaryEmbedding.__init__ does
+    (nanovllm/layers/rotary_embedding.py:28-35)."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float) / head_dim))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1)
+
+
+def rope_case():
+    """q/k RMSNorm + rotary embedding through the reference's own eager code."""
+    from nanovllm.layers.custom_op import CustomOpConfig
+    from nanovllm.layers.layernorm import RMSNorm
+    from nanovllm.layers.rotary_embedding import RotaryEmbedding
+
+    x = rope_inputs()
+    T, Hq, Hkv, D = x["T"], x["Hq"], x["Hkv"], x["D"]
+    q = x["qkv"][:, : Hq * D].view(T, Hq, D)
+    k = x["qkv"][:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    cfg = CustomOpConfig(platform="cpu")
+    eager_rms = RMSNorm._native_rms._torchdynamo_orig_callable
+    norms = []
+    for wgt in (x["q_weight"], x["k_weight"]):
+        norm = RMSNorm(D, eps=x["eps"], custom_op_config=cfg)
+        norm.weight = torch.nn.Parameter(wgt.clone(), requires_grad=False)
+        norms.append(norm)
+    qn = eager_rms(norms[0], q)
+    kn = eager_rms(norms[1], k)
+    rope = RotaryEmbedding(D, D, x["max_position"], x["base"], custom_op_config=cfg)
+    eager_rope = RotaryEmbedding.forward_native._torchdynamo_orig_callable
+    q_rot, k_rot = eager_rope(rope, x["positions"], qn, kn)
+    table = rope.cos_sin_cache.squeeze(1)
+    assert torch.equal(table, rope_cos_sin_cache(D, x["max_position"], x["base"]))
+    return dict(q_rot=bits(q_rot), k_rot=bits(k_rot), q_norm=bits(qn), k_norm=bits(kn),
+                input_digest=digest(x["qkv"], x["positions"], x["q_weight"], x["k_weight"]),
+                table_digest=digest(table))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -193,6 +244,7 @@ def main() -> None:
     np.savez_compressed(HERE / "append_bf16.npz", **append_bf16(KVCacheStore, CustomOpConfig))
     for name in ATTENTION_CASES:
         np.savez_compressed(HERE / f"attn_{name}.npz", **attention_case(reference_fn, name))
+    np.savez_compressed(HERE / "rope.npz", **rope_case())
     np.savez_compressed(HERE / "config1.npz",
                         **config1_case(reference_fn, KVCacheStore, CustomOpConfig))
     print("golden fixtures written to", HERE)
