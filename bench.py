@@ -50,9 +50,13 @@ def parse_args():
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="smaller batches are for profiler captures only")
-    ap.add_argument("--workload", choices=("config2", "config3"), default="config2",
+    ap.add_argument("--workload", choices=("config2", "config3", "rope_append"),
+                    default="config2",
                     help="config3: mixed chunked prefill + decode (1 GPU), reports the "
-                         "prefill kernel against the tensor roofline")
+                         "prefill kernel against the tensor roofline; rope_append: the "
+                         "fused q/k-norm + RoPE + KV append kernel (1 GPU)")
+    ap.add_argument("--rope-tokens", type=int, default=16384,
+                    help="tokens per rope_append step (a long prefill chunk)")
     return ap.parse_args()
 
 
@@ -626,6 +630,105 @@ def run_config3(args):
     print(json.dumps(line), flush=True)
 
 
+def run_rope_append(args):
+    """The step before attention, fused: q/k RMSNorm + neox RoPE + KV append
+    for one layer of Qwen3-8B (Hq 32, Hkv 8, D 128) over --rope-tokens new
+    tokens. Algorithmic bytes per launch: read q, k, v and one cos|sin row per
+    token, write rotated q and the k/v cache rows (weights and metadata are
+    negligible). The engine's unfused chain (q_norm, k_norm, rotary_emb in
+    torch eager, then the append) is timed beside it for context."""
+    from my_vllm_b200 import ops
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    T, Hq, Hkv, D = args.rope_tokens, TOTAL_Q_HEADS, TOTAL_KV_HEADS, HEAD_DIM
+    g = torch.Generator(device=device).manual_seed(4242)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g, device=device).to(torch.bfloat16)
+    q = qkv[:, : Hq * D].view(T, Hq, D)
+    k = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    max_pos = 40960
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float, device=device) / D))
+    freqs = torch.outer(torch.arange(max_pos, dtype=torch.float, device=device), inv_freq)
+    table = torch.cat((freqs.cos(), freqs.sin()), dim=-1).contiguous()
+    positions = torch.randint(0, max_pos, (T,), generator=g, device=device)
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
+    num_blocks = max(2 * T // BLOCK_SIZE, 1)
+    k_cache = torch.zeros(num_blocks, BLOCK_SIZE, Hkv, D, dtype=torch.bfloat16, device=device)
+    v_cache = torch.zeros_like(k_cache)
+    slots = torch.randperm(num_blocks * BLOCK_SIZE, generator=g, device=device)[:T].to(torch.int32)
+    q_out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+    es = 2
+    alg_bytes = (T * (Hq + 2 * Hkv) * D * es) * 2 + T * D * 4
+
+    def fused():
+        ops.qk_norm_rope_append(q, k, v, positions, qw, kw, table, 1e-6, k_cache, v_cache,
+                                slots, q_out)
+
+    def unfused():
+        def norm(x, w):
+            xf = x.float()
+            xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+            return xf.to(x.dtype) * w
+
+        def rope(x):
+            cs = table[positions].unsqueeze(1)
+            cos, sin = cs[..., : D // 2], cs[..., D // 2:]
+            x1, x2 = x.float().chunk(2, dim=-1)
+            return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), -1).to(x.dtype)
+
+        qr = rope(norm(q, qw))
+        kr = rope(norm(k, kw))
+        ops.store_kvcache(kr, v, k_cache, v_cache, slots)
+        return qr
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+    clocks = None if args.no_clocks else ClockSampler(physical_gpu_indices(1))
+    if clocks:
+        clocks.start()
+    t_begin = time.time()
+    ms = timed(fused, args.steps)
+    if clocks:
+        clocks.mark(t_begin, time.time())
+        clocks.stop()
+    unfused_ms = timed(unfused, max(3, args.steps // 4))
+    hbm, src = peaks()
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "fused q/k-norm + RoPE + KV append HBM GB/s", "value": round(gbs, 1),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "tokens_per_s": round(T / (ms * 1e-3), 1),
+        "config": {"workload": f"rope_append: {T} new tokens of Qwen3-8B (Hq 32, Hkv 8, D 128), "
+                               "positions U[0, 40960), rope theta 1e6, bs 16, random slots",
+                   "l2": f"{alg_bytes / 1e6:.0f} MB per launch (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "kernel": "qk_norm_rope_append_kernel",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_source": src,
+                     "algorithmic_bytes_per_launch": alg_bytes},
+        "unfused_torch_eager_ms": round(unfused_ms, 5),
+        "gpu_launches": args.steps,
+    }
+    if clocks:
+        line["clocks"] = clocks.summary()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -636,6 +739,9 @@ def main():
         return
     if args.workload == "config3":
         run_config3(args)
+        return
+    if args.workload == "rope_append":
+        run_rope_append(args)
         return
     if world != args.gpus and "WORLD_SIZE" not in os.environ:
         world = args.gpus

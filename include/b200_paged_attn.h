@@ -97,7 +97,10 @@ B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
  * in fp32 with cos = cos_sin_cache[pos][i], sin = cos_sin_cache[pos][64 + i]
  * and rounds. Slots of -1 skip the cache writes (q is still produced).
  * head_dim must be 128; q/k/v rows may be strided views of the fused qkv
- * projection (heads packed within a row); q_out may alias q.
+ * projection (heads packed within a row); q_out may alias q. Every pointer
+ * (weights and cos_sin_cache included) must be 16-byte aligned and every
+ * stride a multiple of 8 elements. Positions outside [0, max_position) set
+ * B200_STATUS_POSITION_OUT_OF_RANGE and leave that token's q and k unwritten.
  */
 B200_API int b200_qk_norm_rope_append(
     const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,

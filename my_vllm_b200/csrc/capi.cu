@@ -222,14 +222,15 @@ int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_he
       !k_cache || !v_cache || !slot_mapping)
     return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
   if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-        reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(k_cache)) & 3) ||
-      ((reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(v_cache)) & 15) ||
-      (q_token_stride | q_head_stride | k_token_stride | q_out_token_stride |
-       q_out_head_stride) & 1 ||
-      (v_token_stride | cache_slot_stride) & 7)
+        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(q_out) |
+        reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+        reinterpret_cast<uintptr_t>(q_weight) | reinterpret_cast<uintptr_t>(k_weight) |
+        reinterpret_cast<uintptr_t>(cos_sin_cache)) & 15) ||
+      (q_token_stride | q_head_stride | k_token_stride | v_token_stride | q_out_token_stride |
+       q_out_head_stride | cache_slot_stride) & 7)
     return fail(B200_ERR_INVALID_ARGUMENT,
-                "q/k/q_out/k_cache must be 4-byte aligned with even strides; v and v_cache "
-                "16-byte aligned with strides that are multiples of 8");
+                "tensors must be 16-byte aligned with strides that are multiples of 8 "
+                "elements (rows move as 16-byte vectors)");
   if (cache_slot_stride < (int64_t)num_kv_heads * head_dim)
     return fail(B200_ERR_INVALID_ARGUMENT, "cache slot stride must cover all KV heads");
   b200::RopeAppendParams p;

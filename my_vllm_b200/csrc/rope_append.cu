@@ -4,7 +4,7 @@
 // runs q_norm, k_norm (layers/layernorm.py:30-41), the neox-style rotary
 // embedding (layers/rotary_embedding.py:7-15, 40-51) and then the KV append
 // (layers/attention.py:34-41) as separate kernels, each reading and writing
-// q/k through HBM. Here one warp owns one (token, head) row of 128 elements:
+// q/k through HBM. Here one pass over the token's rows does all of it:
 //   q rows: normalise, scale by q_weight, rotate -> q_out
 //   k rows: normalise, scale by k_weight, rotate -> k_cache[slot]
 //   v rows: copied to v_cache[slot]
@@ -20,110 +20,220 @@
 
 namespace b200 {
 
-template <typename T>
-__device__ __forceinline__ float to_f(T x);
-template <>
-__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) {
-  return __bfloat162float(x);
+// ---- packed helpers: a 32-bit word holds two 16-bit elements, a 64-bit
+// register two fp32 values (f32x2 arithmetic, one instruction per pair) ----
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
-template <>
-__device__ __forceinline__ float to_f<__half>(__half x) {
-  return __half2float(x);
+__device__ __forceinline__ void f2_split(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+// Explicit .rn keeps each product and sum separately rounded (no contraction
+// into fused multiply-adds), as the eager fp32 reference computes them.
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
 }
 
 template <typename T>
-__device__ __forceinline__ float round_t(float x) {
-  return to_f<T>(Elem<T>::from_float(x));
+struct Pair;
+template <>
+struct Pair<__nv_bfloat16> {
+  __device__ __forceinline__ static uint64_t widen(uint32_t w) {  // exact
+    return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  __device__ __forceinline__ static uint32_t narrow(uint64_t x) {  // round to nearest even
+    float lo, hi;
+    f2_split(x, lo, hi);
+    return Elem<__nv_bfloat16>::pack(lo, hi);
+  }
+  // 16-bit x 16-bit product rounded once to 16 bits (exact in fp32 first)
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+template <>
+struct Pair<__half> {
+  __device__ __forceinline__ static uint64_t widen(uint32_t w) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return f2(f.x, f.y);
+  }
+  __device__ __forceinline__ static uint32_t narrow(uint64_t x) {
+    float lo, hi;
+    f2_split(x, lo, hi);
+    return Elem<__half>::pack(lo, hi);
+  }
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
+// Work layout: one warp per token; its 32 lanes form 4 groups of 8, each
+// group one (token, head) row per pass: lane l of a group owns elements
+// [8l, 8l + 8) (x1) and [64 + 8l, 64 + 8l + 8) (x2) of the 128-element row,
+// i.e. 8 complete rotary pairs, moved as two 16-byte vectors. The token's
+// cos/sin values stay in registers across its Hq + 2 Hkv rows, the two norm
+// weights in shared memory; the mean of squares is reduced over the group's
+// 8 lanes. Each group loads kRowsInFlight rows before computing any, so
+// every warp keeps 4 KiB of loads in flight.
+constexpr int kRowsInFlight = 4;  // rows each lane group loads before computing
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
     qk_norm_rope_append_kernel(const RopeAppendParams p) {
+  using P = Pair<T>;
+  __shared__ uint4 weights[2][16];  // q_weight, k_weight
+  if (threadIdx.x < 32)
+    weights[threadIdx.x >> 4][threadIdx.x & 15] = __ldg(
+        reinterpret_cast<const uint4*>(threadIdx.x < 16 ? p.q_weight : p.k_weight) +
+        (threadIdx.x & 15));
+  __syncthreads();
+
   const int lane = threadIdx.x & 31;
-  const int64_t rows_per_token = p.num_q_heads + 2 * p.num_kv_heads;
-  const int64_t total = p.num_tokens * rows_per_token;
+  const int grp = lane >> 3;
+  const int l = lane & 7;
+  const uint32_t gmask = 0xffu << (grp * 8);
+  const int hq = p.num_q_heads;
+  const int hqk = p.num_q_heads + p.num_kv_heads;
+  const int rows = hqk + p.num_kv_heads;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < total;
-       r += warps) {
-    const int64_t t = r / rows_per_token;
-    const int j = static_cast<int>(r - t * rows_per_token);
-    const int32_t slot = p.slot_mapping[t];
-    if (j >= p.num_q_heads + p.num_kv_heads) {
-      // v row: plain copy into the cache slot (16 lanes x 16 bytes)
-      if (slot < 0) continue;
-      if (slot >= p.num_slots) {
-        if (lane == 0) report_status(p.status, B200_STATUS_SLOT_OUT_OF_RANGE);
-        continue;
+
+  for (int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+       t < p.num_tokens; t += warps) {
+    const int32_t slot = __ldg(p.slot_mapping + t);
+    const int64_t pos = __ldg(p.positions + t);
+    const bool slot_ok = slot >= 0 && slot < p.num_slots;
+    const bool pos_ok = pos >= 0 && pos < p.max_position;
+    if (lane == 0) {
+      if (slot >= p.num_slots || slot < -1) report_status(p.status, B200_STATUS_SLOT_OUT_OF_RANGE);
+      if (!pos_ok) report_status(p.status, B200_STATUS_POSITION_OUT_OF_RANGE);
+    }
+    uint64_t cs[4], sn[4];  // cos / sin of this lane's 8 pairs, as f32x2
+    if (pos_ok) {
+      const float4* row = reinterpret_cast<const float4*>(p.cos_sin_cache + pos * kRopeHeadDim);
+      const float4 c0 = __ldg(row + 2 * l), c1 = __ldg(row + 2 * l + 1);
+      const float4 s0 = __ldg(row + 16 + 2 * l), s1 = __ldg(row + 16 + 2 * l + 1);
+      cs[0] = f2(c0.x, c0.y); cs[1] = f2(c0.z, c0.w); cs[2] = f2(c1.x, c1.y); cs[3] = f2(c1.z, c1.w);
+      sn[0] = f2(s0.x, s0.y); sn[1] = f2(s0.z, s0.w); sn[2] = f2(s1.x, s1.y); sn[3] = f2(s1.z, s1.w);
+    }
+    // Source row j of this token, or nullptr when nothing is written for it:
+    // k and v rows need a valid slot, q and k rows a valid position.
+    auto src_of = [&](int j) -> const uint4* {
+      if (j >= rows) return nullptr;
+      if (j < hq)
+        return pos_ok ? reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) +
+                                                        t * p.q_token_stride + j * p.q_head_stride)
+                      : nullptr;
+      if (!slot_ok) return nullptr;
+      if (j < hqk)
+        return pos_ok ? reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.k) +
+                                                        t * p.k_token_stride +
+                                                        (j - hq) * kRopeHeadDim)
+                      : nullptr;
+      return reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) +
+                                            t * p.v_token_stride + (j - hqk) * kRopeHeadDim);
+    };
+    for (int j0 = grp; j0 < rows; j0 += 4 * kRowsInFlight) {
+      const uint4* src[kRowsInFlight];
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) src[u] = src_of(j0 + 4 * u);
+      uint4 a[kRowsInFlight], b[kRowsInFlight];
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u)
+        if (src[u]) {
+          a[u] = __ldg(src[u] + l);
+          b[u] = __ldg(src[u] + 8 + l);
+        }
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        if (!src[u]) continue;
+        const int j = j0 + 4 * u;
+        if (j >= hqk) {  // v row: copied into the cache slot unchanged
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) +
+                                                (int64_t)slot * p.cache_slot_stride +
+                                                (j - hqk) * kRopeHeadDim);
+          dst[l] = a[u];
+          dst[8 + l] = b[u];
+          continue;
+        }
+        const bool is_q = j < hq;
+        uint64_t x1[4], x2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x1[i] = P::widen(word(a[u], i));
+          x2[i] = P::widen(word(b[u], i));
+        }
+        // mean of squares over the 128 elements (the group's 8 lanes)
+        uint64_t acc = f2_mul(x1[0], x1[0]);
+#pragma unroll
+        for (int i = 1; i < 4; ++i) acc = f2_fma(x1[i], x1[i], acc);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc = f2_fma(x2[i], x2[i], acc);
+        float ss_lo, ss_hi;
+        f2_split(acc, ss_lo, ss_hi);
+        float ss = ss_lo + ss_hi;
+        ss += __shfl_xor_sync(gmask, ss, 1);
+        ss += __shfl_xor_sync(gmask, ss, 2);
+        ss += __shfl_xor_sync(gmask, ss, 4);
+        const float var = ss * (1.0f / kRopeHeadDim);  // exact: power of two
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+        const uint64_t inv2 = f2(inv, inv);
+        const uint4 w1 = weights[is_q ? 0 : 1][l];
+        const uint4 w2 = weights[is_q ? 0 : 1][8 + l];
+        uint32_t y1w[4], y2w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          // normalise, round to T, scale by the T weight (one rounding), widen
+          const uint64_t n1 = P::widen(P::mul(P::narrow(f2_mul(x1[i], inv2)), word(w1, i)));
+          const uint64_t n2 = P::widen(P::mul(P::narrow(f2_mul(x2[i], inv2)), word(w2, i)));
+          // y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin (fp32, each op rounded)
+          y1w[i] = P::narrow(f2_sub(f2_mul(n1, cs[i]), f2_mul(n2, sn[i])));
+          y2w[i] = P::narrow(f2_add(f2_mul(n2, cs[i]), f2_mul(n1, sn[i])));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(
+            is_q ? reinterpret_cast<T*>(p.q_out) + t * p.q_out_token_stride +
+                       j * p.q_out_head_stride
+                 : reinterpret_cast<T*>(p.k_cache) + (int64_t)slot * p.cache_slot_stride +
+                       (j - hq) * kRopeHeadDim);
+        dst[l] = make_uint4(y1w[0], y1w[1], y1w[2], y1w[3]);
+        dst[8 + l] = make_uint4(y2w[0], y2w[1], y2w[2], y2w[3]);
       }
-      const int h = j - p.num_q_heads - p.num_kv_heads;
-      const T* src = reinterpret_cast<const T*>(p.v) + t * p.v_token_stride + h * kRopeHeadDim;
-      T* dst = reinterpret_cast<T*>(p.v_cache) + (int64_t)slot * p.cache_slot_stride +
-               h * kRopeHeadDim;
-      if (lane < 16)
-        reinterpret_cast<uint4*>(dst)[lane] = __ldg(reinterpret_cast<const uint4*>(src) + lane);
-      continue;
     }
-    const bool is_q = j < p.num_q_heads;
-    const int h = is_q ? j : j - p.num_q_heads;
-    if (!is_q && slot < 0) continue;
-    if (!is_q && slot >= p.num_slots) {
-      if (lane == 0) report_status(p.status, B200_STATUS_SLOT_OUT_OF_RANGE);
-      continue;
-    }
-    const T* src = is_q ? reinterpret_cast<const T*>(p.q) + t * p.q_token_stride +
-                              h * p.q_head_stride
-                        : reinterpret_cast<const T*>(p.k) + t * p.k_token_stride +
-                              h * kRopeHeadDim;
-    // lane owns rotary pairs i = 2*lane, 2*lane + 1: x1 = row[i], x2 = row[64 + i]
-    const int i0 = 2 * lane;
-    const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t*>(src + i0));
-    const uint32_t w2 = __ldg(reinterpret_cast<const uint32_t*>(src + 64 + i0));
-    const T* e1 = reinterpret_cast<const T*>(&w1);
-    const T* e2 = reinterpret_cast<const T*>(&w2);
-    float x[4] = {to_f<T>(e1[0]), to_f<T>(e1[1]), to_f<T>(e2[0]), to_f<T>(e2[1])};
-    float ss = __fmul_rn(x[0], x[0]);
-    ss = __fadd_rn(ss, __fmul_rn(x[1], x[1]));
-    ss = __fadd_rn(ss, __fmul_rn(x[2], x[2]));
-    ss = __fadd_rn(ss, __fmul_rn(x[3], x[3]));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-    const float var = __fdiv_rn(ss, static_cast<float>(kRopeHeadDim));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-    const T* wt = reinterpret_cast<const T*>(is_q ? p.q_weight : p.k_weight);
-    const int dims[4] = {i0, i0 + 1, 64 + i0, 64 + i0 + 1};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float normed = round_t<T>(__fmul_rn(x[e], inv));
-      x[e] = round_t<T>(__fmul_rn(normed, to_f<T>(wt[dims[e]])));
-    }
-    const int64_t pos = p.positions[t];
-    if (pos < 0 || pos >= p.max_position) {  // no rotation row for it: skip, report
-      if (lane == 0) report_status(p.status, B200_STATUS_POSITION_OUT_OF_RANGE);
-      continue;
-    }
-    const float* cs = p.cos_sin_cache + pos * kRopeHeadDim;
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float c = cs[i0 + e];
-      const float s = cs[64 + i0 + e];
-      y[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(x[2 + e], s));      // x1 cos - x2 sin
-      y[2 + e] = __fadd_rn(__fmul_rn(x[2 + e], c), __fmul_rn(x[e], s));  // x2 cos + x1 sin
-    }
-    T* dst = is_q ? reinterpret_cast<T*>(p.q_out) + t * p.q_out_token_stride +
-                        h * p.q_out_head_stride
-                  : reinterpret_cast<T*>(p.k_cache) + (int64_t)slot * p.cache_slot_stride +
-                        h * kRopeHeadDim;
-    *reinterpret_cast<uint32_t*>(dst + i0) = Elem<T>::pack(y[0], y[1]);
-    *reinterpret_cast<uint32_t*>(dst + 64 + i0) = Elem<T>::pack(y[2], y[3]);
   }
 }
 
 cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype,
                                        cudaStream_t stream) {
-  const int64_t rows = p.num_tokens * (p.num_q_heads + 2 * p.num_kv_heads);
-  int64_t blocks = (rows + 7) / 8;  // 8 warps per block, one row per warp
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  // 8 warps per block, one token per warp; at most the 2 blocks per SM that
+  // fit at once, the grid-stride loop covers the rest
+  int64_t blocks = (p.num_tokens + 7) / 8;
+  if (blocks > 148 * 2) blocks = 148 * 2;
   if (blocks < 1) blocks = 1;
   if (dtype == B200_DTYPE_BFLOAT16)
     qk_norm_rope_append_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(p);
