@@ -53,6 +53,9 @@ extern "C" {
 /* element types of Q / K / V / O */
 #define B200_DTYPE_FLOAT16 0
 #define B200_DTYPE_BFLOAT16 1
+/* FP8 E4M3 (1 sign, 4 exponent bits of bias 7, 3 mantissa bits; finite
+ * values up to +-448, no infinities): a KV-cache storage type only. */
+#define B200_DTYPE_FP8_E4M3 2
 
 /* Version of this ABI (major * 100 + minor). */
 B200_API int b200_abi_version(void);
@@ -82,6 +85,26 @@ B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
                        int64_t num_tokens, int64_t row_elems,
                        int32_t elem_bytes, int64_t num_slots,
                        int32_t* status, void* stream);
+
+/*
+ * KV append into an FP8 E4M3 cache (see b200_paged_cache.kv_fp8). No
+ * counterpart in the reference. For every token i with a slot s != -1:
+ *   k_cache[s][e] = fp8(key[i][e] / *k_scale), v_cache[s][e] = fp8(value[i][e] / *v_scale)
+ * for e < row_elems, where x / scale is the IEEE fp32 quotient (scale NULL = 1)
+ * and fp8() rounds to nearest even, saturating to +-448 (NaN stays NaN).
+ * key/value: 16-bit rows of `src_dtype` with row strides in elements;
+ * caches: one byte per element, cache_slot_stride bytes between slots.
+ * row_elems must be a multiple of 16; rows, strides and caches 16-byte
+ * aligned. Slots outside [0, num_slots) other than -1 are skipped and
+ * reported as B200_STATUS_SLOT_OUT_OF_RANGE.
+ */
+B200_API int b200_store_kvcache_fp8(const void* key, int64_t key_row_stride,
+                                    const void* value, int64_t value_row_stride,
+                                    int32_t src_dtype, void* k_cache, void* v_cache,
+                                    int64_t cache_slot_stride, const int32_t* slot_mapping,
+                                    int64_t num_tokens, int64_t row_elems,
+                                    const float* k_scale, const float* v_scale,
+                                    int64_t num_slots, int32_t* status, void* stream);
 
 /*
  * Fused q/k RMSNorm + rotary embedding + KV append: the step before attention
@@ -127,9 +150,18 @@ B200_API int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_
                                      int32_t* slot_mapping, void* stream);
 
 /*
- * Paged KV cache description (NHD). Strides are in elements; the innermost
- * (head_dim) stride is 1. Every stride must be a multiple of 8 elements and
- * both base pointers 16-byte aligned (TMA rules).
+ * Paged KV cache description (NHD). Strides are in elements of the cache's
+ * storage type; the innermost (head_dim) stride is 1. Every stride must be a
+ * multiple of 16 bytes and both base pointers 16-byte aligned (TMA rules).
+ *
+ * kv_fp8 = 0: K and V are stored in `dtype`, the type of Q and O.
+ * kv_fp8 = 1: K and V are stored as FP8 E4M3 (one byte per element), written
+ *   by b200_store_kvcache_fp8; the real values are stored x *k_scale and
+ *   stored x *v_scale (device fp32 scalars, NULL = 1). Q and O stay in
+ *   `dtype`. No counterpart in the reference, whose contract accepts only
+ *   16-bit caches (nanovllm/layers/attention_backend.py:516-519); the layout
+ *   is its [num_blocks, block_size, num_kv_heads, head_dim]
+ *   (nanovllm/engine/model_runner.py:346) with one byte per element.
  */
 typedef struct b200_paged_cache {
   const void* k_cache;
@@ -138,10 +170,13 @@ typedef struct b200_paged_cache {
   int32_t block_size;   /* multiple of 16 */
   int32_t num_kv_heads;
   int32_t head_dim;     /* 128 */
-  int32_t dtype;        /* B200_DTYPE_* */
+  int32_t dtype;        /* B200_DTYPE_FLOAT16 / B200_DTYPE_BFLOAT16: Q, O (and K, V unless kv_fp8) */
   int64_t block_stride; /* elements between consecutive blocks */
   int64_t slot_stride;  /* elements between consecutive slots of a block */
   int64_t head_stride;  /* elements between consecutive KV heads */
+  int32_t kv_fp8;       /* 1: K/V stored as B200_DTYPE_FP8_E4M3 */
+  const float* k_scale; /* kv_fp8 only: dequantisation scales (device), NULL = 1 */
+  const float* v_scale;
 } b200_paged_cache;
 
 /*

@@ -27,6 +27,9 @@ STATUS_POSITION_OUT_OF_RANGE = 0x20
 
 DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
+DTYPE_FP8_E4M3 = 2
+
+ABI_VERSION = 200
 
 # Size of the scratch array built into the library for
 # b200_paged_decode_noalloc (B200_NOALLOC_DECODE_SCRATCH_BYTES).
@@ -37,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "b200_abi_version",
     "b200_last_error",
     "b200_store_kvcache",
+    "b200_store_kvcache_fp8",
     "b200_build_slot_mapping",
     "b200_qk_norm_rope_append",
     "b200_paged_decode_plan",
@@ -60,6 +64,9 @@ class PagedCache(ctypes.Structure):
         ("block_stride", ctypes.c_int64),
         ("slot_stride", ctypes.c_int64),
         ("head_stride", ctypes.c_int64),
+        ("kv_fp8", ctypes.c_int32),
+        ("k_scale", ctypes.c_void_p),
+        ("v_scale", ctypes.c_void_p),
     ]
 
 
@@ -86,6 +93,10 @@ _SIGNATURES = {
     "b200_last_error": ([], ctypes.c_char_p),
     "b200_store_kvcache": (
         [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _I32, _I64, _I64, _I32, _I64, _VP, _VP],
+        _I32,
+    ),
+    "b200_store_kvcache_fp8": (
+        [_VP, _I64, _VP, _I64, _I32, _VP, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _I64, _VP, _VP],
         _I32,
     ),
     "b200_build_slot_mapping": ([_VP, _I64, _VP, _VP, _I32, _I32, _I32, _VP, _VP], _I32),
@@ -145,6 +156,12 @@ def load_library() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argtypes
             fn.restype = restype
+        version = lib.b200_abi_version()
+        if version // 100 != ABI_VERSION // 100:
+            raise RuntimeError(
+                f"{LIBRARY_PATH} has ABI {version}, this binding expects {ABI_VERSION}: rebuild it "
+                "(`python -m my_vllm_b200.build`)"
+            )
         _lib = lib
         return lib
 

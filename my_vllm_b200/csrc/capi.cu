@@ -73,8 +73,11 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash>& map_cache() {
   return m;
 }
 
+int cache_elem_bytes(const b200_paged_cache& c) { return c.kv_fp8 ? 1 : 2; }
+
 // Tensor map over one paged cache tensor viewed as (head_dim, kv_head, slot,
-// block), box = 64 elements x 1 head x 16 slots x 1 block, 128-byte swizzle.
+// block), 128-byte swizzle; box = 64 elements (16-bit) or 128 elements
+// (FP8) x 1 head x 16 slots x 1 block, i.e. 128-byte rows either way.
 int cache_tensor_map(const void* base, const b200_paged_cache& c, CUtensorMap* out) {
   MapKey key;
   std::memset(&key, 0, sizeof(key));
@@ -86,7 +89,7 @@ int cache_tensor_map(const void* base, const b200_paged_cache& c, CUtensorMap* o
   key.strides[0] = c.head_stride;
   key.strides[1] = c.slot_stride;
   key.strides[2] = c.block_stride;
-  key.dtype = c.dtype;
+  key.dtype = c.kv_fp8 ? B200_DTYPE_FP8_E4M3 : c.dtype;
   {
     std::lock_guard<std::mutex> lock(g_map_mu);
     auto it = map_cache().find(key);
@@ -100,15 +103,17 @@ int cache_tensor_map(const void* base, const b200_paged_cache& c, CUtensorMap* o
     return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const cuuint64_t dims[4] = {(cuuint64_t)c.head_dim, (cuuint64_t)c.num_kv_heads,
                               (cuuint64_t)c.block_size, (cuuint64_t)c.num_blocks};
-  const cuuint64_t strides[3] = {(cuuint64_t)c.head_stride * 2, (cuuint64_t)c.slot_stride * 2,
-                                 (cuuint64_t)c.block_stride * 2};
-  const cuuint32_t box[4] = {64, 1, (cuuint32_t)b200::kTileTokens, 1};
+  const cuuint64_t eb = (cuuint64_t)cache_elem_bytes(c);
+  const cuuint64_t strides[3] = {(cuuint64_t)c.head_stride * eb, (cuuint64_t)c.slot_stride * eb,
+                                 (cuuint64_t)c.block_stride * eb};
+  const cuuint32_t box[4] = {(cuuint32_t)(128 / eb), 1, (cuuint32_t)b200::kTileTokens, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType type = c.kv_fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : c.dtype == B200_DTYPE_BFLOAT16
+                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap m;
-  CUresult r = fn(&m,
-                  c.dtype == B200_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  4, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(&m, type, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -128,7 +133,11 @@ int validate_cache(const b200_paged_cache* c) {
   if (c->k_cache == nullptr || c->v_cache == nullptr)
     return fail(B200_ERR_INVALID_ARGUMENT, "key and value caches must both be present");
   if (c->dtype != B200_DTYPE_BFLOAT16 && c->dtype != B200_DTYPE_FLOAT16)
-    return fail(B200_ERR_UNSUPPORTED, "cache dtype must be float16 or bfloat16");
+    return fail(B200_ERR_UNSUPPORTED, "dtype must be float16 or bfloat16");
+  if (c->kv_fp8 != 0 && c->kv_fp8 != 1)
+    return fail(B200_ERR_INVALID_ARGUMENT, "kv_fp8 must be 0 or 1");
+  if (!c->kv_fp8 && (c->k_scale != nullptr || c->v_scale != nullptr))
+    return fail(B200_ERR_INVALID_ARGUMENT, "k_scale / v_scale apply to FP8 caches only");
   if (c->head_dim != b200::kHeadDim)
     return fail(B200_ERR_UNSUPPORTED, "head_dim must be 128");
   if (c->block_size <= 0 || c->block_size % b200::kTileTokens != 0)
@@ -140,10 +149,11 @@ int validate_cache(const b200_paged_cache* c) {
   if (((reinterpret_cast<uintptr_t>(c->k_cache) | reinterpret_cast<uintptr_t>(c->v_cache)) &
        15) != 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "cache base pointers must be 16-byte aligned");
-  if (c->head_stride % 8 || c->slot_stride % 8 || c->block_stride % 8 ||
+  const int64_t per16 = 16 / cache_elem_bytes(*c);  // elements per 16 bytes
+  if (c->head_stride % per16 || c->slot_stride % per16 || c->block_stride % per16 ||
       c->head_stride <= 0 || c->slot_stride <= 0 || c->block_stride <= 0)
     return fail(B200_ERR_INVALID_ARGUMENT,
-                "cache strides must be positive multiples of 8 elements (16 bytes)");
+                "cache strides must be positive multiples of 16 bytes");
   return B200_OK;
 }
 
@@ -172,7 +182,7 @@ void set_last_error(const std::string& message) { g_last_error = message; }
 
 extern "C" {
 
-int b200_abi_version(void) { return 100; }
+int b200_abi_version(void) { return 200; }
 
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -280,6 +290,39 @@ int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_str
                                                   block_size, slot_mapping,
                                                   static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "slot mapping launch");
+  return B200_OK;
+}
+
+int b200_store_kvcache_fp8(const void* key, int64_t key_row_stride, const void* value,
+                           int64_t value_row_stride, int32_t src_dtype, void* k_cache,
+                           void* v_cache, int64_t cache_slot_stride, const int32_t* slot_mapping,
+                           int64_t num_tokens, int64_t row_elems, const float* k_scale,
+                           const float* v_scale, int64_t num_slots, int32_t* status,
+                           void* stream) {
+  g_last_error.clear();
+  if (src_dtype != B200_DTYPE_BFLOAT16 && src_dtype != B200_DTYPE_FLOAT16)
+    return fail(B200_ERR_UNSUPPORTED, "source rows must be float16 or bfloat16");
+  if (num_tokens < 0 || row_elems <= 0 || num_slots < 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be non-negative");
+  if (row_elems % 16)
+    return fail(B200_ERR_INVALID_ARGUMENT, "row_elems must be a multiple of 16");
+  if (num_tokens == 0) return B200_OK;
+  if (!key || !value || !k_cache || !v_cache || !slot_mapping)
+    return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  if (((reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value) |
+        reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) ||
+      (key_row_stride | value_row_stride) % 8 || cache_slot_stride % 16)
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "rows and caches must be 16-byte aligned (row strides multiples of 8 "
+                "elements, cache slot stride a multiple of 16 bytes)");
+  if (cache_slot_stride < row_elems)
+    return fail(B200_ERR_INVALID_ARGUMENT, "cache slot stride must cover a row");
+  cudaError_t e = b200::launch_kv_append_fp8(key, key_row_stride, value, value_row_stride,
+                                             src_dtype, k_cache, v_cache, cache_slot_stride,
+                                             slot_mapping, num_tokens, row_elems, k_scale,
+                                             v_scale, num_slots, status,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 KV append launch");
   return B200_OK;
 }
 
@@ -395,9 +438,12 @@ int b200_paged_decode(const void* q, int64_t q_seq_stride, int64_t q_head_stride
   p.num_q_heads = num_q_heads;
   p.num_blocks = cache->num_blocks;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.k_scale = cache->k_scale;
+  p.v_scale = cache->v_scale;
   p.status = status;
-  cudaError_t e = b200::launch_paged_decode(mk, mv, p, cache->dtype, cache->num_kv_heads,
-                                            num_seqs, static_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      b200::launch_paged_decode(mk, mv, p, cache->dtype, cache->kv_fp8 != 0,
+                                cache->num_kv_heads, num_seqs, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged decode launch");
   return B200_OK;
 }
@@ -412,6 +458,8 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   g_last_error.clear();
   int rc = validate_cache(cache);
   if (rc != B200_OK) return rc;
+  if (cache->kv_fp8)
+    return fail(B200_ERR_UNSUPPORTED, "paged prefill reads 16-bit caches only");
   if (num_seqs < 0 || num_q_tokens < 0 || max_q_len < 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
   if (num_seqs == 0 || num_q_tokens == 0) return B200_OK;

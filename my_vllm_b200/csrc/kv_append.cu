@@ -130,6 +130,96 @@ cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
                        slot64, num_tokens, row_bytes, num_slots, status, stream);
 }
 
+// Append into an FP8 E4M3 cache: each thread quantises 16 consecutive
+// elements of one K or V row (two 16-byte loads, one 16-byte store):
+// stored = e4m3(x / scale), IEEE quotient, round to nearest even with
+// saturation to +-448 (cvt.rn.satfinite; NaN stays NaN).
+template <typename T>
+__device__ __forceinline__ float2 widen2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 widen2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 widen2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// two floats -> two E4M3 bytes (lo in the low byte)
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    kv_append_fp8_kernel(const T* __restrict__ key, int64_t key_row_stride,
+                         const T* __restrict__ value, int64_t value_row_stride,
+                         uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+                         int64_t cache_slot_stride, const int32_t* __restrict__ slot_mapping,
+                         int64_t num_tokens, int64_t vecs_per_row, const float* k_scale,
+                         const float* v_scale, int64_t num_slots, int32_t* status) {
+  const float ks = k_scale != nullptr ? __ldg(k_scale) : 1.f;
+  const float vs = v_scale != nullptr ? __ldg(v_scale) : 1.f;
+  const int64_t per_token = 2 * vecs_per_row;
+  const int64_t total = num_tokens * per_token;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t token = idx / per_token;
+    const int64_t rem = idx - token * per_token;
+    const int is_v = rem >= vecs_per_row;
+    const int64_t vec = rem - (is_v ? vecs_per_row : 0);
+    const int64_t slot = slot_mapping[token];
+    if (slot == -1) continue;
+    if (slot < 0 || slot >= num_slots) {
+      if (vec == 0 && !is_v) report_status(status, B200_STATUS_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(
+        (is_v ? value + token * value_row_stride : key + token * key_row_stride) + vec * 16);
+    const uint4 a = __ldg(src), b = __ldg(src + 1);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const float sc = is_v ? vs : ks;
+    uint32_t out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x0 = widen2<T>(w[2 * i]);
+      const float2 x1 = widen2<T>(w[2 * i + 1]);
+      const uint32_t lo = e4m3x2(__fdiv_rn(x0.x, sc), __fdiv_rn(x0.y, sc));
+      const uint32_t hi = e4m3x2(__fdiv_rn(x1.x, sc), __fdiv_rn(x1.y, sc));
+      out[i] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>((is_v ? v_cache : k_cache) + slot * cache_slot_stride + vec * 16) =
+        make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+cudaError_t launch_kv_append_fp8(const void* key, int64_t key_row_stride, const void* value,
+                                 int64_t value_row_stride, int src_dtype, void* k_cache,
+                                 void* v_cache, int64_t cache_slot_stride,
+                                 const int32_t* slot_mapping, int64_t num_tokens,
+                                 int64_t row_elems, const float* k_scale, const float* v_scale,
+                                 int64_t num_slots, int32_t* status, cudaStream_t stream) {
+  const int64_t vecs = row_elems / 16;
+  const int64_t total = num_tokens * 2 * vecs;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  if (src_dtype == B200_DTYPE_BFLOAT16)
+    kv_append_fp8_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(key), key_row_stride,
+        static_cast<const __nv_bfloat16*>(value), value_row_stride,
+        static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache), cache_slot_stride,
+        slot_mapping, num_tokens, vecs, k_scale, v_scale, num_slots, status);
+  else
+    kv_append_fp8_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const __half*>(key), key_row_stride, static_cast<const __half*>(value),
+        value_row_stride, static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache),
+        cache_slot_stride, slot_mapping, num_tokens, vecs, k_scale, v_scale, num_slots, status);
+  return cudaGetLastError();
+}
+
 // Slot of every new token, from the batch metadata (see b200_build_slot_mapping).
 __global__ void __launch_bounds__(256)
     build_slot_mapping_kernel(const int32_t* __restrict__ block_tables, int64_t bt_stride,

@@ -28,6 +28,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "paged_decode.cuh"
 
@@ -45,16 +47,55 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int valid) {
   return v & (lo | hi);
 }
 
-template <typename T, bool kHiRows>
+// Four FP8 E4M3 values (bytes 0..3) -> two fp16 pairs, exactly: lo holds
+// bytes 0, 1 and hi bytes 2, 3 (low byte -> low half).
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n"
+      " cvt.rn.f16x2.e4m3x2 %1, b;\n}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
+}
+
+__device__ __forceinline__ uint32_t to_f16_pair(uint32_t w, __half) { return w; }
+__device__ __forceinline__ uint32_t to_f16_pair(uint32_t w, __nv_bfloat16) {
+  const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xffff0000u);
+  return Elem<__half>::pack(lo, hi);
+}
+
+template <bool kFp8, typename T>
+__device__ __forceinline__ uint32_t to_f16_or_same(uint32_t w, T tag) {
+  if constexpr (kFp8) return to_f16_pair(w, tag);
+  else return w;
+}
+
+// kFp8 = false: K/V tiles in T, QK^T and PV on T MMAs.
+// kFp8 = true: K/V stored as FP8 E4M3; each 16-token tile is one 2 KiB TMA
+// box per tensor. E4M3 values convert exactly to fp16, so the MMAs run in
+// fp16: q is converted once (exact for |q| in [2^-14, 65504]), P is packed
+// as fp16, and the dequantisation scales fold into the softmax scale (K)
+// and the final normalisation (V). Fragment layouts for FP8:
+//   K: ldmatrix (no transpose) over 16-byte rows gives lane (g, q) the 4
+//      bytes d = 16c + 4q .. 4q+3 of token g; they serve as the B fragment's
+//      k indices {2q, 2q+1} and {8+2q, 9+2q}, so the q fragment is loaded
+//      with the same permutation of d within each 16-element chunk c.
+//   V: ldmatrix.trans at 16-bit granularity gives lane (g, q) the byte pairs
+//      (d = 16c + 2g, 16c + 2g + 1) of tokens 2q and 2q+1; one byte permute
+//      regroups them by d, giving B fragments for column d = 16c + 2g (even
+//      MMA) and 16c + 2g + 1 (odd MMA). The accumulator of chunk c's even
+//      and odd MMAs together holds d = 16c + 4q .. 16c + 4q + 3.
+template <typename T, bool kHiRows, bool kFp8>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v,
                         const DecodeParams p) {
+  using M = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
+  constexpr int kStages = kFp8 ? kFp8Stages : kDecodeStages;
+  constexpr int kStageBytes = kFp8 ? kFp8StageBytes : kDecodeStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeStageArenaBytes);
-  int32_t* bt_s = reinterpret_cast<int32_t*>(bars + kDecodeWarps * kDecodeStages);
+  int32_t* bt_s = reinterpret_cast<int32_t*>(bars + kDecodeWarps * kDecodeMaxStages);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -92,7 +133,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
-    for (int i = 0; i < kDecodeWarps * kDecodeStages; ++i)
+    for (int i = 0; i < kDecodeWarps * kStages; ++i)
       mbar_init(smem_u32(&bars[i]), 1);
     mbar_init_fence();
   }
@@ -106,29 +147,40 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   uint32_t qa[8][4];
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    const int d0 = kk * 16 + tq * 2;
+    // 16-bit caches: k pairs (2q, 2q+1) and (8+2q, 9+2q) of chunk kk are
+    // d = 16kk + 2q (+1) and 16kk + 8 + 2q (+1). FP8: d = 16kk + 4q .. 4q+3.
+    const int d0 = kFp8 ? kk * 16 + tq * 4 : kk * 16 + tq * 2;
+    const int d1 = kFp8 ? d0 + 2 : d0 + 8;
     const bool lo_ok = gr < p.group;
-    qa[kk][0] = lo_ok ? ld_u32(qb + gr * p.q_head_stride + d0) : 0u;
-    qa[kk][2] = lo_ok ? ld_u32(qb + gr * p.q_head_stride + d0 + 8) : 0u;
+    qa[kk][0] = lo_ok ? to_f16_or_same<kFp8>(ld_u32(qb + gr * p.q_head_stride + d0), T()) : 0u;
+    qa[kk][2] = lo_ok ? to_f16_or_same<kFp8>(ld_u32(qb + gr * p.q_head_stride + d1), T()) : 0u;
     if (kHiRows) {
       const bool hi_ok = gr + 8 < p.group;
-      qa[kk][1] = hi_ok ? ld_u32(qb + (gr + 8) * p.q_head_stride + d0) : 0u;
-      qa[kk][3] = hi_ok ? ld_u32(qb + (gr + 8) * p.q_head_stride + d0 + 8) : 0u;
+      qa[kk][1] =
+          hi_ok ? to_f16_or_same<kFp8>(ld_u32(qb + (gr + 8) * p.q_head_stride + d0), T()) : 0u;
+      qa[kk][3] =
+          hi_ok ? to_f16_or_same<kFp8>(ld_u32(qb + (gr + 8) * p.q_head_stride + d1), T()) : 0u;
     } else {
       qa[kk][1] = 0u;
       qa[kk][3] = 0u;
     }
   }
+  float scale_log2 = p.scale_log2;
+  float out_scale = 1.f;
+  if (kFp8) {
+    if (p.k_scale != nullptr) scale_log2 *= __ldg(p.k_scale);
+    if (p.v_scale != nullptr) out_scale = __ldg(p.v_scale);
+  }
 
   // ---- per-warp TMA ring ----
   const int my_tiles =
       ntiles > warp ? (ntiles - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
-  uint8_t* ring = smem + warp * kDecodeStages * kDecodeStageBytes;
+  uint8_t* ring = smem + warp * kStages * kStageBytes;
   const uint32_t ring_u32 = smem_u32(ring);
-  const uint32_t bar0 = smem_u32(&bars[warp * kDecodeStages]);
+  const uint32_t bar0 = smem_u32(&bars[warp * kStages]);
 
   auto issue = [&](int j) {
-    const int stage = j % kDecodeStages;
+    const int stage = j % kStages;
     const int t = warp + j * kDecodeWarps;
     const int tok = tok_begin + t * kTileTokens;
     const int page = bt_s[tok / p.block_size - page_begin];
@@ -136,16 +188,21 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     if (page < 0 || page >= p.num_blocks)
       report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
     // Out-of-range coordinates are zero-filled by TMA, never dereferenced.
-    const uint32_t dst = ring_u32 + stage * kDecodeStageBytes;
+    const uint32_t dst = ring_u32 + stage * kStageBytes;
     const uint32_t bar = bar0 + stage * 8;
-    mbar_arrive_expect_tx(bar, kDecodeStageBytes);
-    tma_load_4d(dst, &tmap_k, bar, 0, kvh, row, page);
-    tma_load_4d(dst + kHalfTileBytes, &tmap_k, bar, 64, kvh, row, page);
-    tma_load_4d(dst + 2 * kHalfTileBytes, &tmap_v, bar, 0, kvh, row, page);
-    tma_load_4d(dst + 3 * kHalfTileBytes, &tmap_v, bar, 64, kvh, row, page);
+    mbar_arrive_expect_tx(bar, kStageBytes);
+    if constexpr (kFp8) {
+      tma_load_4d(dst, &tmap_k, bar, 0, kvh, row, page);
+      tma_load_4d(dst + kFp8TileBytes, &tmap_v, bar, 0, kvh, row, page);
+    } else {
+      tma_load_4d(dst, &tmap_k, bar, 0, kvh, row, page);
+      tma_load_4d(dst + kHalfTileBytes, &tmap_k, bar, 64, kvh, row, page);
+      tma_load_4d(dst + 2 * kHalfTileBytes, &tmap_v, bar, 0, kvh, row, page);
+      tma_load_4d(dst + 3 * kHalfTileBytes, &tmap_v, bar, 64, kvh, row, page);
+    }
   };
 
-  const int prologue = my_tiles < kDecodeStages ? my_tiles : kDecodeStages;
+  const int prologue = my_tiles < kStages ? my_tiles : kStages;
   if (lane == 0)
     for (int j = 0; j < prologue; ++j) issue(j);
   int issued = prologue;
@@ -159,16 +216,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   int consumed = 0;
   bool ok = true;
   for (int j = 0; j < my_tiles; ++j) {
-    const int stage = j % kDecodeStages;
-    const uint32_t parity = (j / kDecodeStages) & 1;
+    const int stage = j % kStages;
+    const uint32_t parity = (j / kStages) & 1;
     const bool got = mbar_wait(bar0 + stage * 8, parity);
     if (!__all_sync(0xffffffffu, got)) {
       ok = false;
       break;
     }
     consumed = j + 1;
-    const uint32_t kb = ring_u32 + stage * kDecodeStageBytes;
-    const uint32_t vb = kb + 2 * kHalfTileBytes;
+    const uint32_t kb = ring_u32 + stage * kStageBytes;
+    const uint32_t vb = kb + (kFp8 ? kFp8TileBytes : 2 * kHalfTileBytes);
     const int t = warp + j * kDecodeWarps;
     const int valid = min(kTileTokens, tok_end - (tok_begin + t * kTileTokens));
 
@@ -178,20 +235,37 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     {
       const int r = (lane & 7) + ((lane >> 4) << 3);
       const int csel = (lane >> 3) & 1;
+      if constexpr (kFp8) {
+        // matrices: (tokens 0-7 | 8-15) x (chunk cc | cc+1) of 16 d each
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t addr = kb + (kk >> 2) * kHalfTileBytes +
-                              swz128(r, ((kk & 3) << 1) + csel);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(addr, b0, b1, b2, b3);
-        Elem<T>::mma(s0, qa[kk], b0, b1);
-        Elem<T>::mma(s1, qa[kk], b2, b3);
+        for (int cc = 0; cc < 8; cc += 2) {
+          uint32_t r0, r1, r2, r3, b0, b1;
+          ldmatrix_x4(kb + swz128(r, cc + csel), r0, r1, r2, r3);
+          e4m3x4_to_f16(r0, b0, b1);
+          Elem<M>::mma(s0, qa[cc], b0, b1);
+          e4m3x4_to_f16(r1, b0, b1);
+          Elem<M>::mma(s0, qa[cc + 1], b0, b1);
+          e4m3x4_to_f16(r2, b0, b1);
+          Elem<M>::mma(s1, qa[cc], b0, b1);
+          e4m3x4_to_f16(r3, b0, b1);
+          Elem<M>::mma(s1, qa[cc + 1], b0, b1);
+        }
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t addr = kb + (kk >> 2) * kHalfTileBytes +
+                                swz128(r, ((kk & 3) << 1) + csel);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(addr, b0, b1, b2, b3);
+          Elem<M>::mma(s0, qa[kk], b0, b1);
+          Elem<M>::mma(s1, qa[kk], b2, b3);
+        }
       }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      s0[i] *= p.scale_log2;
-      s1[i] *= p.scale_log2;
+      s0[i] *= scale_log2;
+      s1[i] *= scale_log2;
     }
     if (valid < kTileTokens) {
       const int c0 = tq * 2;
@@ -220,8 +294,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
         o[n][0] *= alpha;
         o[n][1] *= alpha;
       }
-      pa[0] = Elem<T>::pack(p0, p1);
-      pa[2] = Elem<T>::pack(p2, p3);
+      pa[0] = Elem<M>::pack(p0, p1);
+      pa[2] = Elem<M>::pack(p2, p3);
     }
     if (kHiRows) {
       float mx = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
@@ -239,15 +313,39 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
         o[n][2] *= alpha;
         o[n][3] *= alpha;
       }
-      pa[1] = Elem<T>::pack(p0, p1);
-      pa[3] = Elem<T>::pack(p2, p3);
+      pa[1] = Elem<M>::pack(p0, p1);
+      pa[3] = Elem<M>::pack(p2, p3);
     } else {
       pa[1] = 0u;
       pa[3] = 0u;
     }
 
     // ---- O += P V (16 rows x 128 dims) ----
-    {
+    if constexpr (kFp8) {
+      const int r = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int csel = lane >> 4;
+#pragma unroll
+      for (int cc = 0; cc < 8; cc += 2) {
+        // v0 / v1: tokens 0-7 / 8-15 of chunk cc; v2 / v3: the same of cc+1
+        uint32_t v[4];
+        ldmatrix_x4_trans(vb + swz128(r, cc + csel), v[0], v[1], v[2], v[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t e0, o0, e1, o1;  // even / odd d column, tokens 2q.. / 8+2q..
+          e4m3x4_to_f16(__byte_perm(v[2 * h], 0, 0x3120), e0, o0);
+          e4m3x4_to_f16(__byte_perm(v[2 * h + 1], 0, 0x3120), e1, o1);
+          if (valid < kTileTokens) {
+            // never-written slots past the sequence end may hold NaN bytes
+            e0 = mask_pair(e0, tq * 2, valid);
+            o0 = mask_pair(o0, tq * 2, valid);
+            e1 = mask_pair(e1, 8 + tq * 2, valid);
+            o1 = mask_pair(o1, 8 + tq * 2, valid);
+          }
+          Elem<M>::mma(o[2 * (cc + h)], pa, e0, e1);
+          Elem<M>::mma(o[2 * (cc + h) + 1], pa, o0, o1);
+        }
+      }
+    } else {
       const int r = (lane & 7) + (((lane >> 3) & 1) << 3);
       const int csel = lane >> 4;
 #pragma unroll
@@ -266,12 +364,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
           v1 = mask_pair(v1, 8 + tq * 2, valid);
           v3 = mask_pair(v3, 8 + tq * 2, valid);
         }
-        Elem<T>::mma(o[2 * dn], pa, v0, v1);
-        Elem<T>::mma(o[2 * dn + 1], pa, v2, v3);
+        Elem<M>::mma(o[2 * dn], pa, v0, v1);
+        Elem<M>::mma(o[2 * dn + 1], pa, v2, v3);
       }
     }
 
-    // ---- refill this stage with the warp's tile j + kDecodeStages ----
+    // ---- refill this stage with the warp's tile j + kStages ----
     fence_proxy_async_smem();
     __syncwarp();
     if (issued < my_tiles) {
@@ -285,7 +383,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     // (each wait bounded again) so no TMA writes into smem after exit.
     if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
     for (int j = consumed; j < issued; ++j)
-      mbar_wait(bar0 + (j % kDecodeStages) * 8, (j / kDecodeStages) & 1);
+      mbar_wait(bar0 + (j % kStages) * 8, (j / kStages) & 1);
   }
 
   // ---- merge the warps' partial softmax states ----
@@ -307,15 +405,28 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       ml[warp * 32 + 16 + gr + 8] = l_hi;
     }
   }
+  if constexpr (kFp8) {
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int d = n * 8 + tq * 2;
-    if (gr < p.group)
-      *reinterpret_cast<float2*>(&mo[(warp * 16 + gr) * kMergeStride + d]) =
-          make_float2(o[n][0], o[n][1]);
-    if (kHiRows && gr + 8 < p.group)
-      *reinterpret_cast<float2*>(&mo[(warp * 16 + gr + 8) * kMergeStride + d]) =
-          make_float2(o[n][2], o[n][3]);
+    for (int c = 0; c < 8; ++c) {
+      const int d = c * 16 + tq * 4;
+      if (gr < p.group)
+        *reinterpret_cast<float4*>(&mo[(warp * 16 + gr) * kMergeStride + d]) =
+            make_float4(o[2 * c][0], o[2 * c + 1][0], o[2 * c][1], o[2 * c + 1][1]);
+      if (kHiRows && gr + 8 < p.group)
+        *reinterpret_cast<float4*>(&mo[(warp * 16 + gr + 8) * kMergeStride + d]) =
+            make_float4(o[2 * c][2], o[2 * c + 1][2], o[2 * c][3], o[2 * c + 1][3]);
+    }
+  } else {
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int d = n * 8 + tq * 2;
+      if (gr < p.group)
+        *reinterpret_cast<float2*>(&mo[(warp * 16 + gr) * kMergeStride + d]) =
+            make_float2(o[n][0], o[n][1]);
+      if (kHiRows && gr + 8 < p.group)
+        *reinterpret_cast<float2*>(&mo[(warp * 16 + gr + 8) * kMergeStride + d]) =
+            make_float2(o[n][2], o[n][3]);
+    }
   }
   __syncthreads();
 
@@ -334,7 +445,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       acc += mo[(w * 16 + row) * kMergeStride + d] * sc;
       l += ml[w * 32 + 16 + row] * sc;
     }
-    const float val = l > 0.f ? acc / l : 0.f;
+    const float val = l > 0.f ? acc / l * out_scale : 0.f;
     const int head = kvh * p.group + row;
     if (p.num_parts == 1) {
       T* ob = reinterpret_cast<T*>(p.out) + (int64_t)b * p.out_seq_stride +
@@ -375,11 +486,11 @@ __global__ void __launch_bounds__(kHeadDim)
   ob[d] = Elem<T>::from_float(l > 0.f ? acc / l : 0.f);
 }
 
-template <typename T, bool kHiRows>
+template <typename T, bool kHiRows, bool kFp8>
 static cudaError_t launch_typed(const CUtensorMap& mk, const CUtensorMap& mv,
                                 const DecodeParams& p, int num_kv_heads,
                                 int num_seqs, cudaStream_t stream) {
-  auto kernel = paged_decode_kernel<T, kHiRows>;
+  auto kernel = paged_decode_kernel<T, kHiRows, kFp8>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel),
                                    kDecodeSmemBytes);
   if (e != cudaSuccess) return e;
@@ -394,25 +505,32 @@ static cudaError_t launch_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   return e;
 }
 
-cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
-                                const DecodeParams& p, int dtype,
-                                int num_kv_heads, int num_seqs,
-                                cudaStream_t stream) {
+template <bool kFp8>
+static cudaError_t launch_kv(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeParams& p,
+                             int dtype, int num_kv_heads, int num_seqs, cudaStream_t stream) {
   const bool hi = p.group > 8;
   if (dtype == B200_DTYPE_BFLOAT16)
-    return hi ? launch_typed<__nv_bfloat16, true>(mk, mv, p, num_kv_heads, num_seqs, stream)
-              : launch_typed<__nv_bfloat16, false>(mk, mv, p, num_kv_heads, num_seqs, stream);
-  return hi ? launch_typed<__half, true>(mk, mv, p, num_kv_heads, num_seqs, stream)
-            : launch_typed<__half, false>(mk, mv, p, num_kv_heads, num_seqs, stream);
+    return hi ? launch_typed<__nv_bfloat16, true, kFp8>(mk, mv, p, num_kv_heads, num_seqs, stream)
+              : launch_typed<__nv_bfloat16, false, kFp8>(mk, mv, p, num_kv_heads, num_seqs,
+                                                         stream);
+  return hi ? launch_typed<__half, true, kFp8>(mk, mv, p, num_kv_heads, num_seqs, stream)
+            : launch_typed<__half, false, kFp8>(mk, mv, p, num_kv_heads, num_seqs, stream);
+}
+
+cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
+                                const DecodeParams& p, int dtype, bool kv_fp8,
+                                int num_kv_heads, int num_seqs, cudaStream_t stream) {
+  return kv_fp8 ? launch_kv<true>(mk, mv, p, dtype, num_kv_heads, num_seqs, stream)
+                : launch_kv<false>(mk, mv, p, dtype, num_kv_heads, num_seqs, stream);
 }
 
 int decode_ctas_per_sm() {
   int n = 0;
   const void* kernel =
-      reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, false>);
+      reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, false, false>);
   if (ensure_smem_attr(kernel, kDecodeSmemBytes) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &n, paged_decode_kernel<__nv_bfloat16, false>, kDecodeWarps * 32,
+          &n, paged_decode_kernel<__nv_bfloat16, false, false>, kDecodeWarps * 32,
           kDecodeSmemBytes) != cudaSuccess ||
       n <= 0) {
     cudaGetLastError();

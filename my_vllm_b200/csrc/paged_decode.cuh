@@ -14,12 +14,20 @@ constexpr int kDecodeWarps = 4;
 constexpr int kDecodeStages = 3;
 constexpr int kDecodeStageBytes = 4 * kHalfTileBytes;  // K lo/hi + V lo/hi = 8 KiB
 constexpr int kDecodeStageArenaBytes = kDecodeWarps * kDecodeStages * kDecodeStageBytes;
+// FP8 E4M3 caches: a 16-token tile of K (or V) is 16 rows x 128 bytes, one TMA
+// box; twice as many stages keep the same bytes in flight per warp.
+constexpr int kFp8TileBytes = kTileTokens * 128;
+constexpr int kFp8Stages = 6;
+constexpr int kFp8StageBytes = 2 * kFp8TileBytes;  // K + V = 4 KiB
+static_assert(kDecodeWarps * kFp8Stages * kFp8StageBytes == kDecodeStageArenaBytes,
+              "both cache types share one stage arena");
+constexpr int kDecodeMaxStages = kFp8Stages;
 // Longest KV partition one CTA takes; the planner splits longer contexts.
 constexpr int kMaxPartTokens = 8192;
 constexpr int kMaxPartPages = kMaxPartTokens / kTileTokens + 8;
 constexpr int kMergeStride = kHeadDim + 4;  // padded fp32 row in the merge area
 constexpr int kDecodeSmemBytes = 1024 /* alignment slack */ + kDecodeStageArenaBytes +
-                                 kDecodeWarps * kDecodeStages * 8 + kMaxPartPages * 4;
+                                 kDecodeWarps * kDecodeMaxStages * 8 + kMaxPartPages * 4;
 static_assert(kDecodeWarps * (32 + 16 * kMergeStride) * 4 <= kDecodeStageArenaBytes,
               "merge area must fit in the stage arena");
 
@@ -42,12 +50,14 @@ struct DecodeParams {
   int num_q_heads;
   int64_t num_blocks;
   float scale_log2;  // softmax_scale * log2(e)
+  const float* k_scale;  // FP8 caches: dequantisation scales (nullptr = 1)
+  const float* v_scale;
   int32_t* status;
 };
 
 cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
-                                const DecodeParams& p, int dtype, int num_kv_heads,
-                                int num_seqs, cudaStream_t stream);
+                                const DecodeParams& p, int dtype, bool kv_fp8,
+                                int num_kv_heads, int num_seqs, cudaStream_t stream);
 int decode_ctas_per_sm();
 
 cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
@@ -56,6 +66,13 @@ cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
                              const void* slot_mapping, bool slot64, int64_t num_tokens,
                              int64_t row_elems, int32_t elem_bytes, int64_t num_slots,
                              int32_t* status, cudaStream_t stream);
+
+cudaError_t launch_kv_append_fp8(const void* key, int64_t key_row_stride, const void* value,
+                                 int64_t value_row_stride, int src_dtype, void* k_cache,
+                                 void* v_cache, int64_t cache_slot_stride,
+                                 const int32_t* slot_mapping, int64_t num_tokens,
+                                 int64_t row_elems, const float* k_scale, const float* v_scale,
+                                 int64_t num_slots, int32_t* status, cudaStream_t stream);
 
 cudaError_t launch_build_slot_mapping(const int32_t* block_tables, int64_t bt_stride,
                                       const int32_t* seq_lens, const int32_t* query_start_loc,

@@ -15,6 +15,7 @@ import torch
 from . import _native
 
 _DTYPES = {torch.float16: _native.DTYPE_FLOAT16, torch.bfloat16: _native.DTYPE_BFLOAT16}
+FP8_DTYPE = torch.float8_e4m3fn  # storage type of FP8 KV caches
 
 
 def _stream_handle(device: torch.device) -> int:
@@ -85,6 +86,54 @@ def store_kvcache(
         _ptr(status), _stream_handle(key.device),
     )
     _native.check(rc, "b200_store_kvcache")
+
+
+def store_kvcache_fp8(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
+    *,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Quantise K/V rows into FP8 E4M3 cache slots: ``cache = e4m3(x / scale)``
+    (IEEE quotient, round to nearest even, saturate to +-448); slots of -1
+    are skipped. The FP8 counterpart of ``store_kvcache``; ``k_scale`` and
+    ``v_scale`` are 1-element float32 CUDA tensors (None = 1)."""
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    for name, t in (("key", key), ("value", value), ("k_cache", k_cache),
+                    ("v_cache", v_cache), ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t)
+    if key.dtype not in _DTYPES or value.dtype != key.dtype:
+        raise TypeError("key and value must share one float16/bfloat16 dtype")
+    if k_cache.dtype != FP8_DTYPE or v_cache.dtype != FP8_DTYPE:
+        raise TypeError("FP8 caches must be torch.float8_e4m3fn")
+    if value.shape != key.shape or key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError("key and value must be [tokens, num_kv_heads, head_dim], head_dim contiguous")
+    if key.stride(1) != head_dim or value.stride(1) != head_dim:
+        raise ValueError("key/value heads must be packed (stride(1) == head_dim)")
+    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("key and value caches must have the same shape and strides")
+    if k_cache.stride(1) != D or k_cache.stride(0) != k_cache.size(1) * D:
+        raise ValueError("cache must be packed [num_blocks, block_size, num_kv_heads, head_dim]")
+    if slot_mapping.dtype != torch.int32 or slot_mapping.numel() != N:
+        raise ValueError("slot_mapping must be int32 with one slot per token")
+    for name, t in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if t is not None and (t.dtype != torch.float32 or t.numel() != 1 or t.device.type != "cuda"):
+            raise TypeError(f"{name} must be a 1-element float32 CUDA tensor")
+    if N == 0:
+        return
+    rc = _native.load_library().b200_store_kvcache_fp8(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), _DTYPES[key.dtype],
+        k_cache.data_ptr(), v_cache.data_ptr(), D, slot_mapping.data_ptr(), N, D,
+        _ptr(k_scale), _ptr(v_scale), k_cache.size(0) * k_cache.size(1), _ptr(status),
+        _stream_handle(key.device),
+    )
+    _native.check(rc, "b200_store_kvcache_fp8")
 
 
 def qk_norm_rope_append(
@@ -192,16 +241,23 @@ def build_slot_mapping(
     return out
 
 
-def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.PagedCache:
+def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     q_dtype: torch.dtype | None = None, k_scale: torch.Tensor | None = None,
+                     v_scale: torch.Tensor | None = None) -> _native.PagedCache:
     """Describe a pair of NHD caches ``[num_blocks, block_size, Hkv, D]``.
 
-    Descriptors are cached by (pointers, shape, strides, dtype): layers reuse
-    the same cache views every step, so the checks run once per view."""
+    16-bit caches hold K/V in the query's dtype. FP8 caches
+    (``torch.float8_e4m3fn``) need ``q_dtype`` (float16/bfloat16: the type of
+    q and the output) and take optional 1-element float32 dequantisation
+    scales. Descriptors are cached by (pointers, shape, strides, dtypes,
+    scales): layers reuse the same cache views every step, so the checks run
+    once per view."""
     key = (k_cache.data_ptr(), v_cache.data_ptr(), tuple(k_cache.shape), tuple(v_cache.shape),
-           k_cache.stride(), v_cache.stride(), k_cache.dtype, v_cache.dtype)
+           k_cache.stride(), v_cache.stride(), k_cache.dtype, v_cache.dtype, q_dtype,
+           _ptr(k_scale), _ptr(v_scale))
     desc = _CACHE_DESCS.get(key)
     if desc is None:
-        desc = _make_cache_desc(k_cache, v_cache)
+        desc = _make_cache_desc(k_cache, v_cache, q_dtype, k_scale, v_scale)
         if len(_CACHE_DESCS) > 4096:
             _CACHE_DESCS.clear()
         _CACHE_DESCS[key] = desc
@@ -211,21 +267,40 @@ def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.Pa
 _CACHE_DESCS: dict = {}
 
 
-def _make_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor) -> _native.PagedCache:
+def _make_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor, q_dtype, k_scale,
+                     v_scale) -> _native.PagedCache:
     if k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
         raise ValueError(
             "key and value caches must have shape [pages, block_size, num_kv_heads, head_dim]"
         )
     if k_cache.stride() != v_cache.stride():
         raise ValueError("key and value caches must have identical strides")
-    if k_cache.dtype not in _DTYPES or v_cache.dtype != k_cache.dtype:
-        raise TypeError("caches must be float16 or bfloat16")
+    if v_cache.dtype != k_cache.dtype:
+        raise TypeError("key and value caches must share one dtype")
     if k_cache.stride(3) != 1:
         raise ValueError("cache head_dim must be contiguous")
+    fp8 = k_cache.dtype == FP8_DTYPE
+    if fp8:
+        if q_dtype not in _DTYPES:
+            raise TypeError("an FP8 cache needs the float16/bfloat16 query dtype")
+        for name, t in (("k_scale", k_scale), ("v_scale", v_scale)):
+            if t is not None and (t.dtype != torch.float32 or t.numel() != 1
+                                  or t.device.type != "cuda"):
+                raise TypeError(f"{name} must be a 1-element float32 CUDA tensor")
+        dtype = _DTYPES[q_dtype]
+    else:
+        if k_cache.dtype not in _DTYPES:
+            raise TypeError("caches must be float16, bfloat16 or float8_e4m3fn")
+        if q_dtype is not None and q_dtype != k_cache.dtype:
+            raise ValueError("query, output and 16-bit caches must share one dtype")
+        if k_scale is not None or v_scale is not None:
+            raise ValueError("k_scale / v_scale apply to FP8 caches only")
+        dtype = _DTYPES[k_cache.dtype]
     return _native.PagedCache(
         k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0), k_cache.size(1),
-        k_cache.size(2), k_cache.size(3), _DTYPES[k_cache.dtype],
-        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        k_cache.size(2), k_cache.size(3), dtype,
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), 1 if fp8 else 0,
+        _ptr(k_scale) if fp8 else None, _ptr(v_scale) if fp8 else None,
     )
 
 
@@ -278,15 +353,18 @@ def paged_decode(
     softmax_scale: float,
     workspace: torch.Tensor | None = None,
     *,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Decode attention for ``q [B, Hq, D]`` into ``out [B, Hq, D]`` (in place)."""
+    """Decode attention for ``q [B, Hq, D]`` into ``out [B, Hq, D]`` (in place).
+    With FP8 caches ``k_scale`` / ``v_scale`` dequantise K and V."""
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
                     ("block_tables", block_tables), ("seq_lens", seq_lens), ("out", out)):
         _require_cuda(name, t)
     if q.dim() != 3 or out.shape != q.shape or q.stride(2) != 1 or out.stride(2) != 1:
         raise ValueError("q and out must be [tokens, num_q_heads, head_dim], head_dim contiguous")
-    if q.dtype != k_cache.dtype or out.dtype != q.dtype:
+    if (q.dtype != k_cache.dtype and k_cache.dtype != FP8_DTYPE) or out.dtype != q.dtype:
         raise ValueError("query, output and caches must share one dtype")
     if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
         raise TypeError("block_tables and seq_lens must be int32")
@@ -295,7 +373,7 @@ def paged_decode(
     B = q.size(0)
     if block_tables.size(0) < B or seq_lens.numel() < B:
         raise ValueError("block_tables / seq_lens must have one row per sequence")
-    cache = paged_cache_desc(k_cache, v_cache)
+    cache = paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)
     ws_ptr, ws_bytes = None, 0
     if plan.workspace_bytes:
         if workspace is None or workspace.numel() * workspace.element_size() < plan.workspace_bytes:

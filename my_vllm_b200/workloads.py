@@ -257,6 +257,17 @@ def small_case(query_lengths, kv_lengths, num_prefill, *, Hq=16, Hkv=4, D=128, b
     return w
 
 
+def ragged_decode(device="cuda", dtype=torch.bfloat16, seed=SEED_BASE + 6, *, batch=40,
+                  ctx=(1, 6000), num_q_heads=32, num_kv_heads=8) -> Workload:
+    """A decode batch with context lengths U[ctx], bs 16, permuted pool."""
+    g = _generator(seed, torch.device("cpu"))
+    lens = torch.randint(ctx[0], ctx[1] + 1, (batch,), generator=g).tolist()
+    pool = sum((c + 15) // 16 for c in lens)
+    return _build("ragged_decode", Hq=num_q_heads, Hkv=num_kv_heads, D=128, bs=16,
+                  ctx_lens=lens, q_lens=[1] * batch, num_prefill=0, pool_blocks=pool, seed=seed,
+                  device=device, dtype=dtype)
+
+
 CONFIGS = {
     "config1": config1,
     "config2": config2,
@@ -264,3 +275,15 @@ CONFIGS = {
     "config4": config4,
     "config5": config5,
 }
+
+
+def to_fp8_cache(cache: torch.Tensor, scale: float, chunk_blocks: int = 4096) -> torch.Tensor:
+    """An FP8 E4M3 copy of a 16-bit cache holding cache / scale (round to
+    nearest even, clamped to +-448), converted in chunks so a full-size pool
+    needs no fp32 copy of itself."""
+    out = torch.empty(cache.shape, dtype=torch.float8_e4m3fn, device=cache.device)
+    for i in range(0, cache.size(0), chunk_blocks):
+        part = cache[i: i + chunk_blocks].float().div_(scale).clamp_(-448.0, 448.0)
+        out[i: i + chunk_blocks] = part.to(torch.float8_e4m3fn)
+    return out
+

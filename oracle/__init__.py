@@ -16,3 +16,4 @@ from .paged_attention import (  # noqa: F401
 )
 from .metadata import slot_mapping  # noqa: F401,E402
 from .rope import cos_sin_cache, rms_norm, rope_neox  # noqa: F401,E402
+from . import fp8  # noqa: F401,E402

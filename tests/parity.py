@@ -46,6 +46,35 @@ def sample_oracle(w, seq_ids, k_cache=None, v_cache=None):
     return out, q_rows
 
 
+def sample_oracle_fp8(w, seq_ids, k8, v8, k_scale, v_scale):
+    """fp32 oracle over FP8 caches: the sampled sequences' pages dequantised
+    (stored x scale), q in fp32; returns (output [rows, Hq, D], rows)."""
+    bs = w.block_size
+    qsl = w.extra["qsl_host"]
+    lens = w.extra["seq_lens_host"]
+    tables = w.block_tables.cpu()
+    pages, new_tables, q_rows, q_lens, kv_lens = [], [], [], [], []
+    for s in seq_ids:
+        count = (lens[s] + bs - 1) // bs
+        new_tables.append(list(range(len(pages), len(pages) + count)))
+        pages += tables[s, :count].tolist()
+        q_rows += list(range(qsl[s], qsl[s + 1]))
+        q_lens.append(qsl[s + 1] - qsl[s])
+        kv_lens.append(lens[s])
+    idx = torch.tensor(pages, dtype=torch.long, device=k8.device)
+    kc = oracle.fp8.dequantize(k8.index_select(0, idx).view(torch.uint8).cpu().numpy(), k_scale)
+    vc = oracle.fp8.dequantize(v8.index_select(0, idx).view(torch.uint8).cpu().numpy(), v_scale)
+    width = max(len(t) for t in new_tables)
+    bt = np.full((len(seq_ids), width), -1, dtype=np.int64)
+    for i, t in enumerate(new_tables):
+        bt[i, : len(t)] = t
+    q = w.q[torch.tensor(q_rows, device=w.q.device)].float().cpu().numpy()
+    qsl_s = np.cumsum([0] + q_lens)
+    out = oracle.paged_attention_from_tables(q, kc, vc, bt, np.array(kv_lens), qsl_s, bs,
+                                             dtype="float32", out_dtype="float32")
+    return out, q_rows
+
+
 def assert_close_to_oracle(actual: torch.Tensor, expected_f32: np.ndarray, dtype) -> float:
     a = actual.detach().float().cpu().numpy()
     err = float(np.max(np.abs(a - expected_f32))) if a.size else 0.0

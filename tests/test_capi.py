@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = _native.load_library()
     for name in _declared_functions():
         assert hasattr(lib, name), name
-    assert lib.b200_abi_version() == 100
+    assert lib.b200_abi_version() == _native.ABI_VERSION
 
 
 def test_plan_without_gpu_falls_back_to_148_sms():
@@ -94,6 +94,39 @@ def test_prefill_and_append_reject_unsupported_shapes():
     # zero tokens is a successful no-op, even with NULL pointers
     assert lib.b200_store_kvcache(None, 1024, None, 1024, None, None, 1024, None, 0, 0, 1024,
                                   2, 64, None, None) == _native.B200_OK
+
+
+def test_fp8_cache_arguments_checked_before_launch():
+    lib = _native.load_library()
+    plan = _native.DecodePlan(1, 4096, 0)
+    # FP8 strides are in bytes: 8-element (8-byte) strides break the 16-byte rule
+    bad = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                             16 * 8 * 128, 8 * 128, 8, 1, None, None)
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, bad, 0x4000, 256, 0x5000, 4, 32,
+                               0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT and b"16 bytes" in lib.b200_last_error()
+    # scales on a 16-bit cache are a caller mistake
+    scaled = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                                16 * 8 * 128, 8 * 128, 128, 0, 0x9000, None)
+    rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, scaled, 0x4000, 256, 0x5000, 4, 32,
+                               0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT and b"FP8" in lib.b200_last_error()
+    # prefill over an FP8 cache is not built yet: refused, nothing launched
+    fp8 = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                             16 * 8 * 128, 8 * 128, 128, 1, None, None)
+    rc = lib.b200_paged_prefill(0x3000, 32 * 128, 128, fp8, 0x4000, 2, 0x5000, 0x6000, 2, 10,
+                                5, 32, 0x7000, 32 * 128, 128, 0.088, None, None)
+    assert rc == _native.B200_ERR_UNSUPPORTED
+    # the FP8 append wants rows of whole 16-byte vectors
+    rc = lib.b200_store_kvcache_fp8(0x1000, 1024, 0x2000, 1024, _native.DTYPE_BFLOAT16, 0x3000,
+                                    0x4000, 1024, 0x5000, 4, 1000, None, None, 64, None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT and b"multiple of 16" in lib.b200_last_error()
+    rc = lib.b200_store_kvcache_fp8(0x1000, 1024, 0x2000, 1024, 7, 0x3000, 0x4000, 1024, 0x5000,
+                                    4, 1024, None, None, 64, None, None)
+    assert rc == _native.B200_ERR_UNSUPPORTED
+    assert lib.b200_store_kvcache_fp8(None, 1024, None, 1024, _native.DTYPE_BFLOAT16, None, None,
+                                      1024, None, 0, 1024, None, None, 64, None,
+                                      None) == _native.B200_OK
 
 
 def test_status_description():
