@@ -55,6 +55,9 @@ def parse_args():
                     help="config3: mixed chunked prefill + decode (1 GPU), reports the "
                          "prefill kernel against the tensor roofline; rope_append: the "
                          "fused q/k-norm + RoPE + KV append kernel (1 GPU)")
+    ap.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
+                    help="fp8: the config 2 step over an FP8 E4M3 KV pool (scales 1.0); "
+                         "bytes are counted at one byte per element")
     ap.add_argument("--rope-tokens", type=int, default=16384,
                     help="tokens per rope_append step (a long prefill chunk)")
     return ap.parse_args()
@@ -279,8 +282,18 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
     w = make_shard(rank, world, device, args.batch)
+    fp8 = args.kv_dtype == "fp8"
+    if fp8:
+        from my_vllm_b200 import workloads
+
+        w.k_cache = workloads.to_fp8_cache(w.k_cache, 1.0)
+        w.v_cache = workloads.to_fp8_cache(w.v_cache, 1.0)
+        torch.cuda.empty_cache()
+        ops.register_kv_scales(w.k_cache, w.v_cache,
+                               torch.ones(1, device=device), torch.ones(1, device=device))
     backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, BLOCK_SIZE,
-                               torch.bfloat16)
+                               torch.bfloat16,
+                               kv_cache_dtype=torch.float8_e4m3fn if fp8 else None)
     common = w.common_metadata()
     plan = backend.build_plan(common)
     kv_bytes = w.kv_bytes_read()
@@ -445,7 +458,7 @@ def run_ours(args, rank, world, local_rank):
         sampler.stop()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not fp8:
         cpu = cpu_baseline_leg(args.cpu_sample_seqs)
 
     graphs.clear()  # release the captured graphs before tearing the process group down
@@ -460,7 +473,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     achieved = kv_bytes * world / (decode_ms_max * 1e-3) / 1e9  # all ranks' decode bytes
     per_gpu_achieved = kv_bytes / (decode_ms * 1e-3) / 1e9
-    traffic = committed_traffic() if world == 1 else None
+    traffic = committed_traffic() if world == 1 and not fp8 else None
     line = {
         "metric": METRIC,
         "value": round(total_bytes / (ms_per_step * 1e-3) / 1e9, 2),
@@ -472,10 +485,10 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16 (KV cache fp8-e4m3)" if fp8 else "bf16",
         "data": "synthetic",
         "config": {
-            "workload": WORKLOAD,
+            "workload": WORKLOAD + (", KV pool FP8 E4M3 (1 byte per element)" if fp8 else ""),
             "global_batch": args.batch,
             "seq_len": CONTEXT,
             "parallelism": f"kv-head shards x{world} (tp{world}), no data-path collective",

@@ -198,8 +198,15 @@ class B200PagedBackend(AttentionBackend):
         dtype: torch.dtype,
         *,
         decode_num_parts: int = 0,
+        kv_cache_dtype: torch.dtype | None = None,
     ) -> None:
         super().__init__(num_q_heads, num_kv_heads, head_dim, block_size, dtype)
+        # Storage type of the paged caches: the activation dtype (the
+        # reference's only option) or FP8 E4M3 with per-layer scales attached
+        # through ops.register_kv_scales.
+        self.kv_cache_dtype = dtype if kv_cache_dtype is None else kv_cache_dtype
+        if self.kv_cache_dtype not in (dtype, ops.FP8_DTYPE):
+            raise TypeError("kv_cache_dtype must be the backend dtype or torch.float8_e4m3fn")
         reason = _static_support_reason(
             num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, head_dim=head_dim,
             block_size=block_size, dtype=dtype,
@@ -386,10 +393,12 @@ class B200PagedBackend(AttentionBackend):
             self._validate_inputs(q, k_cache, v_cache)
             if graph_state.output.shape != q.shape:
                 raise RuntimeError("decode graph attention output does not match query shape")
+            k_scale, v_scale = self._scales(k_cache)
             return ops.paged_decode(
                 q, k_cache, v_cache, graph_state.block_tables, graph_state.seq_lens,
                 graph_state.output, graph_state.decode_plan, self.softmax_scale,
-                graph_state.workspace, status=self.status_tensor(q.device),
+                graph_state.workspace, k_scale=k_scale, v_scale=v_scale,
+                status=self.status_tensor(q.device),
             )
 
         if plan.route is AttentionRoute.WARMUP or not has_k:
@@ -430,12 +439,14 @@ class B200PagedBackend(AttentionBackend):
                 self.softmax_scale, num_seqs=nP, status=status,
             )
 
+        k_scale, v_scale = self._scales(k_cache)
+
         def decode():
             assert metadata.decode_plan is not None
             ops.paged_decode(
                 q[P:], k_cache, v_cache, block_tables[nP:], metadata.seq_lens[nP:],
                 output[P:], metadata.decode_plan, self.softmax_scale, self._workspace,
-                status=status,
+                k_scale=k_scale, v_scale=v_scale, status=status,
             )
 
         if nP and common.num_decode_seqs:
@@ -455,6 +466,11 @@ class B200PagedBackend(AttentionBackend):
         else:
             decode()
         return output
+
+    def _scales(self, k_cache: torch.Tensor):
+        if self.kv_cache_dtype != ops.FP8_DTYPE:
+            return None, None
+        return ops.kv_scales(k_cache)
 
     def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
         stream = self._side_streams.get(device)
@@ -563,8 +579,9 @@ class B200PagedBackend(AttentionBackend):
             raise ValueError("query must have shape [tokens, num_q_heads, head_dim]")
         tail = (self.block_size, self.num_kv_heads, self.head_dim)
         for name, cache in (("key", k_cache), ("value", v_cache)):
-            if cache.device != q.device or cache.dtype != self.dtype:
-                raise ValueError(f"{name} cache must share the query device and dtype")
+            if cache.device != q.device or cache.dtype != self.kv_cache_dtype:
+                raise ValueError(f"{name} cache must be on the query device with the "
+                                 "backend's KV-cache dtype")
             if cache.ndim != 4 or cache.shape[1:] != tail:
                 raise ValueError(
                     f"{name} cache must have shape [pages, block_size, num_kv_heads, head_dim]"

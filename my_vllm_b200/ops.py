@@ -47,8 +47,13 @@ def store_kvcache(
     Drop-in for ``store_kvcache`` (nanovllm/layers/attention.py:34-41): same
     arguments, the same stride assertions (attention.py:37-40), in place, on
     the current stream. ``status`` (int32 CUDA tensor) collects
-    out-of-range-slot reports.
+    out-of-range-slot reports. An FP8 cache (``torch.float8_e4m3fn``) routes
+    to ``store_kvcache_fp8`` with the scales ``register_kv_scales`` attached.
     """
+    if k_cache.dtype == FP8_DTYPE:  # an FP8 pool: quantise with its registered scales
+        store_kvcache_fp8(key, value, k_cache, v_cache, slot_mapping, *kv_scales(k_cache),
+                          status=status)
+        return
     N, num_heads, head_dim = key.shape
     D = num_heads * head_dim
     if not (key.stride(-1) == 1 and value.stride(-1) == 1):
@@ -86,6 +91,27 @@ def store_kvcache(
         _ptr(status), _stream_handle(key.device),
     )
     _native.check(rc, "b200_store_kvcache")
+
+
+_KV_SCALES: dict = {}
+
+
+def register_kv_scales(k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       k_scale: torch.Tensor | None, v_scale: torch.Tensor | None) -> None:
+    """Attach per-layer dequantisation scales to an FP8 cache pair, so the
+    engine-facing calls (``store_kvcache``, the backend's ``forward``), whose
+    signatures carry no scales, find them by the cache's address."""
+    if k_cache.dtype != FP8_DTYPE or v_cache.dtype != FP8_DTYPE:
+        raise TypeError("scales apply to torch.float8_e4m3fn caches only")
+    for name, t in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if t is not None and (t.dtype != torch.float32 or t.numel() != 1 or t.device != k_cache.device):
+            raise TypeError(f"{name} must be a 1-element float32 tensor on the cache's device")
+    _KV_SCALES[k_cache.data_ptr()] = (k_scale, v_scale)
+
+
+def kv_scales(k_cache: torch.Tensor):
+    """(k_scale, v_scale) registered for this FP8 cache, or (None, None) = 1."""
+    return _KV_SCALES.get(k_cache.data_ptr(), (None, None))
 
 
 def store_kvcache_fp8(
@@ -402,6 +428,8 @@ def paged_prefill(
     softmax_scale: float,
     *,
     num_seqs: int | None = None,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Causal paged prefill over ``num_seqs`` sequences into ``out`` (in place)."""
@@ -411,7 +439,7 @@ def paged_prefill(
         _require_cuda(name, t)
     if q.dim() != 3 or out.shape != q.shape or q.stride(2) != 1 or out.stride(2) != 1:
         raise ValueError("q and out must be [tokens, num_q_heads, head_dim], head_dim contiguous")
-    if q.dtype != k_cache.dtype or out.dtype != q.dtype:
+    if (q.dtype != k_cache.dtype and k_cache.dtype != FP8_DTYPE) or out.dtype != q.dtype:
         raise ValueError("query, output and caches must share one dtype")
     for name, t in (("block_tables", block_tables), ("seq_lens", seq_lens),
                     ("query_start_loc", query_start_loc)):
@@ -422,7 +450,7 @@ def paged_prefill(
     S = seq_lens.numel() if num_seqs is None else num_seqs
     if query_start_loc.numel() < S + 1 or block_tables.size(0) < S:
         raise ValueError("query_start_loc / block_tables too short for num_seqs")
-    cache = paged_cache_desc(k_cache, v_cache)
+    cache = paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)
     rc = _native.load_library().b200_paged_prefill(
         q.data_ptr(), q.stride(0), q.stride(1), cache,
         block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(),

@@ -129,3 +129,83 @@ def test_fp8_decode_config2_full_size(cuda_device):
     # deterministic: a second run is bit-identical
     out2, _ = _fp8_decode(w, k8, v8, ks, vs, cuda_device)
     assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+
+
+def test_fp8_backend_decode_route_and_graph(cuda_device):
+    """The engine-facing path with an FP8 pool: store_kvcache (rebound into
+    the engine) dispatches to the quantising append with the registered
+    scales, the backend's decode route reads FP8 pages, and the full-decode
+    CUDA graph captures and replays both."""
+    from my_vllm_b200 import B200PagedBackend
+    from my_vllm_b200.contract import CommonAttentionMetadata
+
+    w = workloads.config2(device=cuda_device, batch=8, ctx=700, pool_blocks=512)
+    ks, vs = 0.05, 0.04
+    k8, v8 = workloads.to_fp8_cache(w.k_cache, ks), workloads.to_fp8_cache(w.v_cache, vs)
+    kst, vst = _scale(ks, cuda_device), _scale(vs, cuda_device)
+    ops.register_kv_scales(k8, v8, kst, vst)
+    backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, 128, 16, torch.bfloat16,
+                               kv_cache_dtype=torch.float8_e4m3fn)
+    ops.store_kvcache(w.key, w.value, k8, v8, w.slot_mapping)
+    # the appended rows hold the quantised new K/V
+    k_ref = k8.view(torch.uint8).cpu().numpy().copy()
+    v_ref = v8.view(torch.uint8).cpu().numpy().copy()
+    oracle.fp8.kv_append_fp8(storage(w.key), storage(w.value), k_ref, v_ref,
+                             w.slot_mapping.cpu().numpy(), ks, vs)
+    assert np.array_equal(k8.view(torch.uint8).cpu().numpy(), k_ref)
+    assert np.array_equal(v8.view(torch.uint8).cpu().numpy(), v_ref)
+
+    plan = backend.build_plan(w.common_metadata())
+    eager = backend.forward(w.q, w.key, w.value, k8, v8, plan).clone()
+    torch.cuda.synchronize()
+    backend.check_status()
+    expected, rows = sample_oracle_fp8(w, list(range(8)), k8, v8, ks, vs)
+    assert_close_to_oracle(eager[rows], expected, w.q.dtype)
+
+    state = backend.create_full_decode_graph_state(8, 8 * 64, cuda_device)
+    static_q = torch.zeros_like(w.q)
+    static_k = torch.zeros_like(w.key)
+    static_v = torch.zeros_like(w.value)
+    static_slots = torch.full((8,), -1, dtype=torch.int32, device=cuda_device)
+    capture_common = CommonAttentionMetadata(
+        num_prefill_seqs=0, num_decode_seqs=8, num_prefill_tokens=0, num_decode_tokens=8,
+        query_start_loc=torch.arange(9, dtype=torch.int32, device=cuda_device),
+        seq_lens=torch.ones(8, dtype=torch.int32, device=cuda_device),
+        slot_mapping=static_slots,
+        block_tables=torch.zeros(8, 1, dtype=torch.int32, device=cuda_device),
+        max_q_len=1, max_kv_len=1, block_counts=(1,) * 8, num_kv_blocks=8, trusted=True)
+    capture_plan = backend.build_plan(capture_common)
+    backend.plan_full_decode_graph(state, capture_plan)
+    backend.activate_full_decode_graph(state)
+    try:
+        def body():
+            ops.store_kvcache(static_k, static_v, k8, v8, static_slots)
+            return backend.forward(static_q, static_k, static_v, k8, v8, capture_plan)
+        body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            graph_out = body()
+    finally:
+        backend.deactivate_full_decode_graph()
+    backend.plan_full_decode_graph(state, plan)
+    static_q.copy_(w.q)
+    static_k.copy_(w.key)
+    static_v.copy_(w.value)
+    static_slots.copy_(w.slot_mapping)
+    graph.replay()
+    torch.cuda.synchronize()
+    # the graph state plans its own (worst-case) split, so compare with the oracle
+    assert_close_to_oracle(graph_out[rows], expected, w.q.dtype)
+    assert np.array_equal(k8.view(torch.uint8).cpu().numpy(), k_ref)  # re-append: idempotent
+
+
+def test_fp8_prefill_is_refused_not_wrong(cuda_device):
+    """Prefill over an FP8 pool is refused before anything launches."""
+    w = workloads.small_case([5], [40], 1, device=cuda_device)
+    k8 = workloads.to_fp8_cache(w.k_cache, 1.0)
+    v8 = workloads.to_fp8_cache(w.v_cache, 1.0)
+    out = torch.empty_like(w.q)
+    with pytest.raises(RuntimeError, match="16-bit"):
+        ops.paged_prefill(w.q, k8, v8, w.block_tables, w.seq_lens, w.query_start_loc, out, 5,
+                          0.088)
