@@ -84,7 +84,7 @@ __device__ __forceinline__ uint32_t to_f16_or_same(uint32_t w, T tag) {
 //      MMA) and 16c + 2g + 1 (odd MMA). The accumulator of chunk c's even
 //      and odd MMAs together holds d = 16c + 4q .. 16c + 4q + 3.
 template <typename T, bool kHiRows, bool kFp8>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 2)
+__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v,
                         const DecodeParams p) {
@@ -94,8 +94,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeStageArenaBytes);
-  int32_t* bt_s = reinterpret_cast<int32_t*>(bars + kDecodeWarps * kDecodeMaxStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      smem + (kFp8 ? kFp8StageArenaBytes : kDecodeStageArenaBytes));
+  int32_t* bt_s = reinterpret_cast<int32_t*>(bars + kDecodeWarps * kStages);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -288,12 +289,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       const float p0 = fast_exp2(s0[0] - base), p1 = fast_exp2(s0[1] - base);
       const float p2 = fast_exp2(s1[0] - base), p3 = fast_exp2(s1[1] - base);
       l_lo = l_lo * alpha + (p0 + p1) + (p2 + p3);
-      m_lo = m_new;
+      // alpha is exactly 1 unless the running max moved: skip the 32
+      // multiplies on the (usual) tiles where no row's max moved
+      if (__any_sync(0xffffffffu, m_new != m_lo)) {
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][0] *= alpha;
-        o[n][1] *= alpha;
+        for (int n = 0; n < 16; ++n) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+        }
       }
+      m_lo = m_new;
       pa[0] = Elem<M>::pack(p0, p1);
       pa[2] = Elem<M>::pack(p2, p3);
     }
@@ -307,12 +312,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       const float p0 = fast_exp2(s0[2] - base), p1 = fast_exp2(s0[3] - base);
       const float p2 = fast_exp2(s1[2] - base), p3 = fast_exp2(s1[3] - base);
       l_hi = l_hi * alpha + (p0 + p1) + (p2 + p3);
-      m_hi = m_new;
+      if (__any_sync(0xffffffffu, m_new != m_hi)) {
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][2] *= alpha;
-        o[n][3] *= alpha;
+        for (int n = 0; n < 16; ++n) {
+          o[n][2] *= alpha;
+          o[n][3] *= alpha;
+        }
       }
+      m_hi = m_new;
       pa[1] = Elem<M>::pack(p0, p1);
       pa[3] = Elem<M>::pack(p2, p3);
     } else {
@@ -491,11 +498,11 @@ static cudaError_t launch_typed(const CUtensorMap& mk, const CUtensorMap& mv,
                                 const DecodeParams& p, int num_kv_heads,
                                 int num_seqs, cudaStream_t stream) {
   auto kernel = paged_decode_kernel<T, kHiRows, kFp8>;
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel),
-                                   kDecodeSmemBytes);
+  constexpr int kSmem = decode_smem_bytes(kFp8);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.num_parts, num_kv_heads, num_seqs);
-  kernel<<<grid, kDecodeWarps * 32, kDecodeSmemBytes, stream>>>(mk, mv, p);
+  kernel<<<grid, kDecodeWarps * 32, kSmem, stream>>>(mk, mv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.num_parts > 1) {
@@ -522,21 +529,6 @@ cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
                                 int num_kv_heads, int num_seqs, cudaStream_t stream) {
   return kv_fp8 ? launch_kv<true>(mk, mv, p, dtype, num_kv_heads, num_seqs, stream)
                 : launch_kv<false>(mk, mv, p, dtype, num_kv_heads, num_seqs, stream);
-}
-
-int decode_ctas_per_sm() {
-  int n = 0;
-  const void* kernel =
-      reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, false, false>);
-  if (ensure_smem_attr(kernel, kDecodeSmemBytes) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &n, paged_decode_kernel<__nv_bfloat16, false, false>, kDecodeWarps * 32,
-          kDecodeSmemBytes) != cudaSuccess ||
-      n <= 0) {
-    cudaGetLastError();
-    return 2;
-  }
-  return n;
 }
 
 }  // namespace b200

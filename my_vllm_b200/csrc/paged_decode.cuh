@@ -15,21 +15,25 @@ constexpr int kDecodeStages = 3;
 constexpr int kDecodeStageBytes = 4 * kHalfTileBytes;  // K lo/hi + V lo/hi = 8 KiB
 constexpr int kDecodeStageArenaBytes = kDecodeWarps * kDecodeStages * kDecodeStageBytes;
 // FP8 E4M3 caches: a 16-token tile of K (or V) is 16 rows x 128 bytes, one TMA
-// box; twice as many stages keep the same bytes in flight per warp.
+// box. Per-token work is the same as for 16-bit caches but the bytes halve,
+// so the FP8 kernel runs 3 CTAs per SM (more warps to hide MMA and convert
+// latency) with 4 stages of 4 KiB per warp: 192 KiB in flight per SM, as
+// the 16-bit kernel's 2 CTAs x 4 warps x 3 x 8 KiB.
 constexpr int kFp8TileBytes = kTileTokens * 128;
-constexpr int kFp8Stages = 6;
+constexpr int kFp8Stages = 4;
 constexpr int kFp8StageBytes = 2 * kFp8TileBytes;  // K + V = 4 KiB
-static_assert(kDecodeWarps * kFp8Stages * kFp8StageBytes == kDecodeStageArenaBytes,
-              "both cache types share one stage arena");
-constexpr int kDecodeMaxStages = kFp8Stages;
+constexpr int kFp8StageArenaBytes = kDecodeWarps * kFp8Stages * kFp8StageBytes;
 // Longest KV partition one CTA takes; the planner splits longer contexts.
 constexpr int kMaxPartTokens = 8192;
 constexpr int kMaxPartPages = kMaxPartTokens / kTileTokens + 8;
 constexpr int kMergeStride = kHeadDim + 4;  // padded fp32 row in the merge area
-constexpr int kDecodeSmemBytes = 1024 /* alignment slack */ + kDecodeStageArenaBytes +
-                                 kDecodeWarps * kDecodeMaxStages * 8 + kMaxPartPages * 4;
-static_assert(kDecodeWarps * (32 + 16 * kMergeStride) * 4 <= kDecodeStageArenaBytes,
+constexpr int decode_smem_bytes(bool fp8) {
+  return 1024 /* alignment slack */ + (fp8 ? kFp8StageArenaBytes : kDecodeStageArenaBytes) +
+         kDecodeWarps * (fp8 ? kFp8Stages : kDecodeStages) * 8 + kMaxPartPages * 4;
+}
+static_assert(kDecodeWarps * (32 + 16 * kMergeStride) * 4 <= kFp8StageArenaBytes,
               "merge area must fit in the stage arena");
+static_assert(3 * decode_smem_bytes(true) <= 227 * 1024, "3 FP8 CTAs per SM");
 
 struct DecodeParams {
   const void* q;
@@ -58,7 +62,6 @@ struct DecodeParams {
 cudaError_t launch_paged_decode(const CUtensorMap& mk, const CUtensorMap& mv,
                                 const DecodeParams& p, int dtype, bool kv_fp8,
                                 int num_kv_heads, int num_seqs, cudaStream_t stream);
-int decode_ctas_per_sm();
 
 cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
                              const void* value, int64_t value_row_stride,
