@@ -432,14 +432,15 @@ class B200PagedBackend(AttentionBackend):
         if plan.batch_type is not expected:
             raise ValueError("B200 route does not match the planned BatchType")
 
+        k_scale, v_scale = self._scales(k_cache)
+
         def prefill():
             ops.paged_prefill(
                 q[:P], k_cache, v_cache, block_tables[:nP], metadata.seq_lens[:nP],
                 metadata.query_start_loc[: nP + 1], output[:P], common.max_q_len,
-                self.softmax_scale, num_seqs=nP, status=status,
+                self.softmax_scale, num_seqs=nP, k_scale=k_scale, v_scale=v_scale,
+                status=status,
             )
-
-        k_scale, v_scale = self._scales(k_cache)
 
         def decode():
             assert metadata.decode_plan is not None

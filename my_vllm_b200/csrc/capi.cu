@@ -458,8 +458,6 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   g_last_error.clear();
   int rc = validate_cache(cache);
   if (rc != B200_OK) return rc;
-  if (cache->kv_fp8)
-    return fail(B200_ERR_UNSUPPORTED, "paged prefill reads 16-bit caches only");
   if (num_seqs < 0 || num_q_tokens < 0 || max_q_len < 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
   if (num_seqs == 0 || num_q_tokens == 0) return B200_OK;
@@ -493,10 +491,12 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.num_q_heads = num_q_heads;
   p.num_blocks = cache->num_blocks;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.k_scale = cache->k_scale;
+  p.v_scale = cache->v_scale;
   p.status = status;
-  cudaError_t e =
-      b200::launch_paged_prefill_tc(mk, mv, p, cache->dtype, cache->num_kv_heads, num_seqs,
-                                    max_q_len, static_cast<cudaStream_t>(stream));
+  cudaError_t e = b200::launch_paged_prefill_tc(mk, mv, p, cache->dtype, cache->kv_fp8 != 0,
+                                                cache->num_kv_heads, num_seqs, max_q_len,
+                                                static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged prefill launch");
   return B200_OK;
 }

@@ -23,6 +23,8 @@ struct PrefillParams {
   int num_q_heads;
   int64_t num_blocks;
   float scale_log2;  // softmax_scale * log2(e)
+  const float* k_scale;  // FP8 caches: dequantisation scales (nullptr = 1)
+  const float* v_scale;
   int32_t* status;
 };
 
@@ -30,7 +32,8 @@ struct PrefillParams {
 // per CTA on UMMA M = 128 tiles, so the GQA heads of a KV head share every
 // K/V tile the CTA loads.
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
-                                    const PrefillParams& p, int dtype, int num_kv_heads,
-                                    int num_seqs, int max_q_len, cudaStream_t stream);
+                                    const PrefillParams& p, int dtype, bool kv_fp8,
+                                    int num_kv_heads, int num_seqs, int max_q_len,
+                                    cudaStream_t stream);
 
 }  // namespace b200

@@ -36,8 +36,18 @@
 //   * Every mbarrier wait is bounded; on a timeout the CTA reports
 //     B200_STATUS_WAIT_TIMEOUT, drains its TMA loads and MMAs with bounded
 //     waits, frees its tensor memory and exits.
+//   * FP8 E4M3 caches (kFp8): the producer warp TMA-loads each 128-token K or
+//     V tile as 16 KiB of FP8 into a 2-slot staging ring (one tile ahead)
+//     and converts it, exactly, into the same fp16 K-major / N-major tile
+//     layout the MMAs read (E4M3 values are all representable in fp16), then
+//     signals the tile full. Q is staged as fp16 and P packed as fp16, so the
+//     MMAs run kind::f16 on fp16 operands; the K scale folds into the softmax
+//     scale and the V scale into the final normalisation. The K ring has 2
+//     stages instead of 3 to make room for the staging ring.
 #include <cuda_runtime.h>
 #include <math.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "paged_decode.cuh"
@@ -55,13 +65,20 @@ constexpr int kTcMmaWarp = 9;
 constexpr int kTcHalf = kTcRows * 128;          // [128 rows x 64 elements] = 16 KiB
 constexpr int kTcQ = 0;                         // Q_A, Q_B: 2 x 32 KiB
 constexpr int kTcTileBytes = 2 * kTcHalf;       // one K or V tile (lo/hi halves) = 32 KiB
-constexpr int kTcKStages = 3;                   // K is freed after the S MMAs: deeper ring
 constexpr int kTcVStages = 2;                   // V is freed after the PV MMAs
 constexpr int kTcK0 = kTcTiles * kTcTileBytes;
-constexpr int kTcV0 = kTcK0 + kTcKStages * kTcTileBytes;
-constexpr int kTcBars = kTcV0 + kTcVStages * kTcTileBytes;
-constexpr int kTcSmemBytes = 1024 + kTcBars + 256;
-static_assert(kTcSmemBytes <= 227 * 1024, "shared memory budget");
+constexpr int kTcRawTileBytes = kTcKv * 128;    // one FP8 K or V tile = 16 KiB
+// Shared-memory map per cache type: Q_A | Q_B | K ring | V ring | [FP8 staging] | barriers.
+// K is freed after the S MMAs, so a deeper ring lets it run further ahead.
+template <bool kFp8>
+struct TcLayout {
+  static constexpr int kKStages = kFp8 ? 2 : 3;
+  static constexpr int kV0 = kTcK0 + kKStages * kTcTileBytes;
+  static constexpr int kRaw0 = kV0 + kTcVStages * kTcTileBytes;  // FP8 staging, 2 slots
+  static constexpr int kBars = kRaw0 + (kFp8 ? 2 * kTcRawTileBytes : 0);
+  static constexpr int kSmemBytes = 1024 + kBars + 256;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
 constexpr uint32_t kTcTmemCols = 512;           // per tile X: S_X at 256X, O_X at 256X+128
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
@@ -70,17 +87,37 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return Elem<T>::pack(lo, hi);
 }
 
-template <typename T>
+// 16-bit pair of T -> fp16 pair (exact for fp16; bf16 values round to
+// nearest fp16, exact for |x| in [2^-14, 65504] with <= 8 significant bits)
+__device__ __forceinline__ uint32_t pair_to_f16(uint32_t w, __half) { return w; }
+__device__ __forceinline__ uint32_t pair_to_f16(uint32_t w, __nv_bfloat16) {
+  return Elem<__half>::pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// two E4M3 bytes (the low 16 bits of v) -> fp16 pair, exactly
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
+  uint32_t d;
+  asm("{\n .reg .b16 a;\n cvt.u16.u32 a, %1;\n cvt.rn.f16x2.e4m3x2 %0, a;\n}"
+      : "=r"(d)
+      : "r"(v));
+  return d;
+}
+
+template <typename T, bool kFp8>
 __global__ void __launch_bounds__(kTcThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                             const __grid_constant__ CUtensorMap tmap_v,
                             const PrefillParams p) {
+  using L = TcLayout<kFp8>;
+  using M = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
+  constexpr int kTcKStages = L::kKStages;
+  constexpr int kTcV0 = L::kV0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBars);
-  uint64_t* k_full = bars + 0;     // [3] TMA -> MMA
-  uint64_t* k_empty = bars + 3;    // [3] MMA (commit after the S MMAs) -> TMA
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  uint64_t* k_full = bars + 0;     // [<=3] TMA (FP8: the converter) -> MMA
+  uint64_t* k_empty = bars + 3;    // [<=3] MMA (commit after the S MMAs) -> TMA
   uint64_t* v_full = bars + 6;     // [2] TMA -> MMA
   uint64_t* v_empty = bars + 8;    // [2] MMA (commit after the PV MMAs) -> TMA
   uint64_t* s_full = bars + 10;    // [2] per Q tile: MMA (commit) -> softmax
@@ -88,6 +125,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* o_done = bars + 14;    // [2] per Q tile: MMA (commit) -> epilogue
   uint64_t* mma_drain = bars + 16; // MMA (commit) -> MMA, before TMEM is freed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* raw_full = bars + 18;  // [2] FP8 staging: TMA -> converter
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -133,6 +171,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(smem_u32(&o_done[x]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
+    if (kFp8) {
+      mbar_init(smem_u32(&raw_full[0]), 1);
+      mbar_init(smem_u32(&raw_full[1]), 1);
+    }
     mbar_init_fence();
   }
   if (warp == kTcMmaWarp) {
@@ -158,7 +200,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t* qtile = smem + kTcQ + x_tile * 2 * kTcHalf;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      const uint4 v = row_token >= 0 ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+      uint4 v = row_token >= 0 ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+      if (kFp8) {  // the MMAs run on fp16 operands
+        v.x = pair_to_f16(v.x, T());
+        v.y = pair_to_f16(v.y, T());
+        v.z = pair_to_f16(v.z, T());
+        v.w = pair_to_f16(v.w, T());
+      }
       *reinterpret_cast<uint4*>(qtile + (c >> 3) * kTcHalf + swz128(t, c & 7)) = v;
     }
     fence_proxy_async_smem();
@@ -169,7 +217,118 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   bool ok = true;
 
-  if (warp == kTcProducerWarp) {
+  if (warp == kTcProducerWarp && kFp8) {
+    // ------------------------------------------------ FP8 producer/converter --
+    // Items in the 16-bit producer's order: K0, K1, then (V_m, K_{m+2}), then
+    // the last V tiles. Item i is TMA-loaded into staging slot i % 2 one item
+    // ahead, then converted into its fp16 K or V stage.
+    const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
+    const int max_page_idx = (seq_len - 1) / p.block_size;
+    const int k0 = min(2, n_total);
+    const int pairs = max(0, n_total - 2);
+    auto item_at = [&](int i, bool& is_v, int& j) {
+      if (i < k0) {
+        is_v = false;
+        j = i;
+      } else if (i - k0 < 2 * pairs) {
+        const int m = i - k0;
+        is_v = (m & 1) == 0;
+        j = is_v ? m / 2 : m / 2 + 2;
+      } else {
+        is_v = true;
+        j = pairs + (i - k0 - 2 * pairs);
+      }
+    };
+    const int n_items = 2 * n_total;
+    const uint32_t raw0 = sbase + L::kRaw0;
+    auto stage_raw = [&](int i) {  // TMA of item i into staging slot i % 2
+      bool is_v;
+      int j;
+      item_at(i, is_v, j);
+      const uint32_t bar = smem_u32(&raw_full[i & 1]);
+      if (lane == 0) mbar_arrive_expect_tx(bar, kTcRawTileBytes);
+      __syncwarp();
+      if (lane < kTcKv / kTileTokens) {
+        const int tok = j * kTcKv + lane * kTileTokens;
+        int pidx = tok / p.block_size;
+        int row = tok % p.block_size;
+        if (pidx > max_page_idx) {  // past the sequence end: any valid page, masked later
+          pidx = max_page_idx;
+          row = 0;
+        }
+        const int page = bt_row[pidx];
+        if (page < 0 || page >= p.num_blocks)
+          report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
+        tma_load_4d(raw0 + (i & 1) * kTcRawTileBytes + lane * kFp8TileBytes,
+                    is_v ? &tmap_v : &tmap_k, bar, 0, kvh, row, page);
+      }
+    };
+    int staged = 0, converted = 0;
+    if (n_items > 0) {
+      stage_raw(0);
+      staged = 1;
+    }
+    for (int i = 0; i < n_items && ok; ++i) {
+      bool is_v;
+      int j;
+      item_at(i, is_v, j);
+      const int nst = is_v ? kTcVStages : kTcKStages;
+      const int st = j % nst;
+      if (j >= nst) {  // the fp16 stage is free once the MMAs that read it retired
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        const bool got = mbar_wait(smem_u32(&empty[st]), ((j / nst) - 1) & 1);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+      }
+      if (i + 1 < n_items) {  // slot (i+1) % 2 was converted last iteration
+        stage_raw(i + 1);
+        staged = i + 2;
+      }
+      const bool landed = mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
+      if (!__all_sync(0xffffffffu, landed)) {
+        ok = false;
+        break;
+      }
+      converted = i + 1;
+      // 128 rows x 8 chunks of 16 E4M3 values; lane (r % 4, c) of each
+      // 4-row group: chunk c (d = 16c .. 16c + 15) -> fp16 chunks 2c', 2c'+1
+      // of half c / 4, both 128-byte swizzled like the TMA tiles
+      const uint8_t* raw = smem + L::kRaw0 + (i & 1) * kTcRawTileBytes;
+      uint8_t* dst = smem + (is_v ? kTcV0 : kTcK0) + st * kTcTileBytes;
+      const int c = lane & 7;
+      const int h = c >> 2;
+      const int c2 = (c & 3) * 2;
+#pragma unroll 4
+      for (int it = 0; it < kTcKv / 4; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        const uint4 w = *reinterpret_cast<const uint4*>(raw + swz128(r, c));
+        uint4 lo, hi;
+        lo.x = e4m3x2_f16x2(w.x);
+        lo.y = e4m3x2_f16x2(w.x >> 16);
+        lo.z = e4m3x2_f16x2(w.y);
+        lo.w = e4m3x2_f16x2(w.y >> 16);
+        hi.x = e4m3x2_f16x2(w.z);
+        hi.y = e4m3x2_f16x2(w.z >> 16);
+        hi.z = e4m3x2_f16x2(w.w);
+        hi.w = e4m3x2_f16x2(w.w >> 16);
+        uint8_t* drow = dst + h * kTcHalf;
+        *reinterpret_cast<uint4*>(drow + swz128(r, c2)) = lo;
+        *reinterpret_cast<uint4*>(drow + swz128(r, c2 + 1)) = hi;
+      }
+      // generic-proxy writes (the fp16 tile) and reads (the staging slot,
+      // refilled by TMA next) -> async proxy, then hand the tile to the MMA
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(is_v ? &v_full[st] : &k_full[st]));
+    }
+    if (!ok) {
+      if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+      for (int i = converted; i < staged; ++i)  // TMA loads still in flight
+        mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
+    }
+  } else if (warp == kTcProducerWarp) {
     // ------------------------------------------------------------ producer --
     // Issue order K0, K1, then (V_j, K_{j+2}) for j = 0, 1, ...: K runs two
     // tiles ahead (its stage frees as soon as the S MMAs of a tile retire),
@@ -223,7 +382,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == kTcMmaWarp) {
     // ---------------------------------------------------------- MMA issuer --
     if (lane == 0) {
-      constexpr bool kBf16 = Elem<T>::kDtype == B200_DTYPE_BFLOAT16;
+      constexpr bool kBf16 = Elem<M>::kDtype == B200_DTYPE_BFLOAT16;
       const uint32_t idesc_s = f16_instr_desc(kTcRows, kTcKv, kBf16, false);
       const uint32_t idesc_pv = f16_instr_desc(kTcRows, kHeadDim, kBf16, true);
       auto kmajor = [&](uint32_t addr, int k) {  // K-major, 16-element k-step k
@@ -304,6 +463,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int my_tiles = x_tile ? n_b : n_a;
     const float kNegInf = -INFINITY;
     float m_used = kNegInf, l = 0.f;
+    float scale = p.scale_log2;  // FP8: times the K dequantisation scale
+    float out_scale = 1.f;       // FP8: the V dequantisation scale
+    if (kFp8) {
+      if (p.k_scale != nullptr) scale *= __ldg(p.k_scale);
+      if (p.v_scale != nullptr) out_scale = __ldg(p.v_scale);
+    }
     for (int j = 0; j < my_tiles; ++j) {
       const bool got = mbar_wait(smem_u32(&s_full[x_tile]), j & 1);
       if (!__all_sync(0xffffffffu, got)) {
@@ -339,7 +504,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // the softmax scale is positive, so it commutes with the maximum
       const float m_raw = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
                                 fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
-      const float m_tile = m_raw == kNegInf ? kNegInf : m_raw * p.scale_log2;
+      const float m_tile = m_raw == kNegInf ? kNegInf : m_raw * scale;
       float alpha = 1.f;
       bool rescale = false;
       if (m_tile > m_used + kRescaleThreshold) {
@@ -348,7 +513,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         rescale = true;
       }
       const float neg_base = m_used == kNegInf ? 0.f : -m_used;
-      const float scale = p.scale_log2;
       float sk[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -364,7 +528,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             p1 = c * 32 + 2 * i + 1 < lim ? p1 : 0.f;
           }
           sk[i & 3] += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
+          pk[i] = pack2<M>(p0, p1);
         }
         // P over S: chunk c's 32 values -> 16 columns at 16c, which only
         // overlap S columns this row has already read
@@ -413,7 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
     } else if (my_tiles > 0) {
       tc_fence_after_sync();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float inv_l = l > 0.f ? out_scale / l : 0.f;
       T* orow = reinterpret_cast<T*>(p.out) +
                 (int64_t)(q_start + max(row_token, 0)) * p.out_token_stride +
                 (int64_t)row_head * p.out_head_stride;
@@ -444,27 +608,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-template <typename T>
+template <typename T, bool kFp8>
 static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
                                    const PrefillParams& p, int num_kv_heads, int num_seqs,
                                    int max_q_len, cudaStream_t stream) {
-  auto kernel = paged_prefill_tc_kernel<T>;
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kTcSmemBytes);
+  auto kernel = paged_prefill_tc_kernel<T, kFp8>;
+  constexpr int kSmem = TcLayout<kFp8>::kSmemBytes;
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kSmem);
   if (e != cudaSuccess) return e;
   const int tpc = (kTcTiles * kTcRows) / p.group;
   const int blocks = (max_q_len + tpc - 1) / tpc;
   if (blocks <= 0) return cudaSuccess;
   dim3 grid(blocks, num_kv_heads, num_seqs);
-  kernel<<<grid, kTcThreads, kTcSmemBytes, stream>>>(mk, mv, p);
+  kernel<<<grid, kTcThreads, kSmem, stream>>>(mk, mv, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
-                                    const PrefillParams& p, int dtype, int num_kv_heads,
-                                    int num_seqs, int max_q_len, cudaStream_t stream) {
+                                    const PrefillParams& p, int dtype, bool kv_fp8,
+                                    int num_kv_heads, int num_seqs, int max_q_len,
+                                    cudaStream_t stream) {
   if (dtype == B200_DTYPE_BFLOAT16)
-    return launch_tc_typed<__nv_bfloat16>(mk, mv, p, num_kv_heads, num_seqs, max_q_len, stream);
-  return launch_tc_typed<__half>(mk, mv, p, num_kv_heads, num_seqs, max_q_len, stream);
+    return kv_fp8 ? launch_tc_typed<__nv_bfloat16, true>(mk, mv, p, num_kv_heads, num_seqs,
+                                                         max_q_len, stream)
+                  : launch_tc_typed<__nv_bfloat16, false>(mk, mv, p, num_kv_heads, num_seqs,
+                                                          max_q_len, stream);
+  return kv_fp8 ? launch_tc_typed<__half, true>(mk, mv, p, num_kv_heads, num_seqs, max_q_len,
+                                                stream)
+                : launch_tc_typed<__half, false>(mk, mv, p, num_kv_heads, num_seqs, max_q_len,
+                                                 stream);
 }
 
 }  // namespace b200

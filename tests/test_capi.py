@@ -111,8 +111,8 @@ def test_fp8_cache_arguments_checked_before_launch():
     rc = lib.b200_paged_decode(0x3000, 32 * 128, 128, scaled, 0x4000, 256, 0x5000, 4, 32,
                                0x6000, 32 * 128, 128, 0.088, plan, None, 0, None, None)
     assert rc == _native.B200_ERR_INVALID_ARGUMENT and b"FP8" in lib.b200_last_error()
-    # prefill over an FP8 cache is not built yet: refused, nothing launched
-    fp8 = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+    # an FP8 cache still needs a 16-bit query/output type
+    fp8 = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_FP8_E4M3,
                              16 * 8 * 128, 8 * 128, 128, 1, None, None)
     rc = lib.b200_paged_prefill(0x3000, 32 * 128, 128, fp8, 0x4000, 2, 0x5000, 0x6000, 2, 10,
                                 5, 32, 0x7000, 32 * 128, 128, 0.088, None, None)

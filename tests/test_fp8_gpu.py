@@ -200,12 +200,41 @@ def test_fp8_backend_decode_route_and_graph(cuda_device):
     assert np.array_equal(k8.view(torch.uint8).cpu().numpy(), k_ref)  # re-append: idempotent
 
 
-def test_fp8_prefill_is_refused_not_wrong(cuda_device):
-    """Prefill over an FP8 pool is refused before anything launches."""
-    w = workloads.small_case([5], [40], 1, device=cuda_device)
-    k8 = workloads.to_fp8_cache(w.k_cache, 1.0)
-    v8 = workloads.to_fp8_cache(w.v_cache, 1.0)
-    out = torch.empty_like(w.q)
-    with pytest.raises(RuntimeError, match="16-bit"):
-        ops.paged_prefill(w.q, k8, v8, w.block_tables, w.seq_lens, w.query_start_loc, out, 5,
-                          0.088)
+@pytest.mark.parametrize("q_lens,kv_lens", [([5], [40]), ([37, 1, 300], [37, 90, 1100]),
+                                               ([129, 256], [700, 256])])
+def test_fp8_prefill_matches_oracle(cuda_device, q_lens, kv_lens):
+    """Chunked prefill over FP8 pages (prefix hits + new chunk, causal)."""
+    w = workloads.small_case(q_lens, kv_lens, len(q_lens), device=cuda_device)
+    ks, vs = 0.03, 0.02
+    k8, v8 = workloads.to_fp8_cache(w.k_cache, ks), workloads.to_fp8_cache(w.v_cache, vs)
+    out = torch.full_like(w.q, float("nan"))
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ops.paged_prefill(w.q, k8, v8, w.block_tables, w.seq_lens, w.query_start_loc, out,
+                      max(q_lens), 128 ** -0.5, k_scale=_scale(ks, cuda_device),
+                      v_scale=_scale(vs, cuda_device), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    expected, rows = sample_oracle_fp8(w, list(range(len(q_lens))), k8, v8, ks, vs)
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+def test_fp8_config3_mixed_step_through_backend(cuda_device):
+    """Config 3 over an FP8 pool through the backend's MIXED route: the
+    prefill kernel (FP8 staged and converted to fp16 tiles) and the decode
+    kernel run concurrently into one output."""
+    from my_vllm_b200 import B200PagedBackend
+
+    w = workloads.config3(device=cuda_device)
+    ks, vs = 0.02, 0.02
+    k8, v8 = workloads.to_fp8_cache(w.k_cache, ks), workloads.to_fp8_cache(w.v_cache, vs)
+    ops.register_kv_scales(k8, v8, _scale(ks, cuda_device), _scale(vs, cuda_device))
+    backend = B200PagedBackend(32, 8, 128, 16, torch.bfloat16, kv_cache_dtype=torch.float8_e4m3fn)
+    ops.store_kvcache(w.key, w.value, k8, v8, w.slot_mapping)
+    plan = backend.build_plan(w.common_metadata())
+    out = backend.forward(w.q, w.key, w.value, k8, v8, plan).clone()
+    torch.cuda.synchronize()
+    backend.check_status()
+    expected, rows = sample_oracle_fp8(w, [0, 1, 2, 3], k8, v8, ks, vs)
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    expected, rows = sample_oracle_fp8(w, [4, 60, 127], k8, v8, ks, vs)
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
