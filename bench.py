@@ -545,8 +545,17 @@ def run_config3(args):
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     w = workloads.config3(device=device)
+    fp8 = args.kv_dtype == "fp8"
+    scales = {}
+    if fp8:
+        w.k_cache = workloads.to_fp8_cache(w.k_cache, 1.0)
+        w.v_cache = workloads.to_fp8_cache(w.v_cache, 1.0)
+        ones = torch.ones(1, device=device)
+        ops.register_kv_scales(w.k_cache, w.v_cache, ones, ones)
+        scales = {"k_scale": ones, "v_scale": ones}
     backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, BLOCK_SIZE,
-                               torch.bfloat16)
+                               torch.bfloat16,
+                               kv_cache_dtype=torch.float8_e4m3fn if fp8 else None)
     common = w.common_metadata()
     plan = backend.build_plan(common)
     md = plan.metadata
@@ -564,12 +573,12 @@ def run_config3(args):
     def prefill():
         ops.paged_prefill(w.q[:P], w.k_cache, w.v_cache, md.block_tables[:nP],
                           md.seq_lens[:nP], md.query_start_loc[: nP + 1], out[:P],
-                          common.max_q_len, backend.softmax_scale, num_seqs=nP)
+                          common.max_q_len, backend.softmax_scale, num_seqs=nP, **scales)
 
     def decode():
         ops.paged_decode(w.q[P:], w.k_cache, w.v_cache, md.block_tables[nP:],
                          md.seq_lens[nP:], out[P:], md.decode_plan, backend.softmax_scale,
-                         backend._workspace)
+                         backend._workspace, **scales)
 
     def step():  # the engine's MIXED route: decode || prefill on two streams
         ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
@@ -624,10 +633,12 @@ def run_config3(args):
         "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": round(ms, 5), "serial_ms_per_step": round(serial_ms, 5),
         "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "bf16 (KV cache fp8-e4m3)" if fp8 else "bf16",
+        "data": "synthetic",
         "config": {"workload": "config3: 4 x 512-token prefill chunks on shared prefix hits "
                                "0/512/1024/2048 + 124 decode rows ctx U[128, 8192], Qwen3-8B "
-                               "heads, bs 16; append 2172 rows",
+                               "heads, bs 16; append 2172 rows"
+                               + ("; KV pool FP8 E4M3" if fp8 else ""),
                    "l2": "decode streams 2.1 GB per step between prefill launches"},
         "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel",
                      "achieved": round(dec_gbs, 1), "peak": hbm, "unit": "GB/s",

@@ -201,6 +201,15 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// Four FP8 E4M3 values (bytes 0..3) -> two fp16 pairs, exactly: lo holds
+// bytes 0, 1 and hi bytes 2, 3 (low byte -> low half).
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n"
+      " cvt.rn.f16x2.e4m3x2 %1, b;\n}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
+}
+
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
 // 2^x with the MUFU ex2 instruction (ex2.approx.ftz.f32, PTX ISA), for the

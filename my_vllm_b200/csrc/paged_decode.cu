@@ -47,15 +47,6 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok, int valid) {
   return v & (lo | hi);
 }
 
-// Four FP8 E4M3 values (bytes 0..3) -> two fp16 pairs, exactly: lo holds
-// bytes 0, 1 and hi bytes 2, 3 (low byte -> low half).
-__device__ __forceinline__ void e4m3x4_to_f16(uint32_t v, uint32_t& lo, uint32_t& hi) {
-  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n"
-      " cvt.rn.f16x2.e4m3x2 %1, b;\n}"
-      : "=r"(lo), "=r"(hi)
-      : "r"(v));
-}
-
 __device__ __forceinline__ uint32_t to_f16_pair(uint32_t w, __half) { return w; }
 __device__ __forceinline__ uint32_t to_f16_pair(uint32_t w, __nv_bfloat16) {
   const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xffff0000u);

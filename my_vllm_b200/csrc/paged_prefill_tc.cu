@@ -59,9 +59,12 @@ namespace b200 {
 constexpr int kTcRows = 128;   // UMMA M (rows of one Q tile)
 constexpr int kTcTiles = 2;    // Q tiles per CTA
 constexpr int kTcKv = 128;     // KV tokens per tile (N of QK^T, K of PV)
-constexpr int kTcThreads = 320;
 constexpr int kTcProducerWarp = 8;
 constexpr int kTcMmaWarp = 9;
+constexpr int kTcConvWarp0 = 10;  // FP8 only: warps 10 and 11 convert staged tiles
+constexpr int kTcConvWarps = 2;
+template <bool kFp8>
+constexpr int tc_threads() { return (kFp8 ? 12 : 10) * 32; }
 constexpr int kTcHalf = kTcRows * 128;          // [128 rows x 64 elements] = 16 KiB
 constexpr int kTcQ = 0;                         // Q_A, Q_B: 2 x 32 KiB
 constexpr int kTcTileBytes = 2 * kTcHalf;       // one K or V tile (lo/hi halves) = 32 KiB
@@ -94,17 +97,8 @@ __device__ __forceinline__ uint32_t pair_to_f16(uint32_t w, __nv_bfloat16) {
   return Elem<__half>::pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
-// two E4M3 bytes (the low 16 bits of v) -> fp16 pair, exactly
-__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
-  uint32_t d;
-  asm("{\n .reg .b16 a;\n cvt.u16.u32 a, %1;\n cvt.rn.f16x2.e4m3x2 %0, a;\n}"
-      : "=r"(d)
-      : "r"(v));
-  return d;
-}
-
 template <typename T, bool kFp8>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                             const __grid_constant__ CUtensorMap tmap_v,
                             const PrefillParams p) {
@@ -125,7 +119,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* o_done = bars + 14;    // [2] per Q tile: MMA (commit) -> epilogue
   uint64_t* mma_drain = bars + 16; // MMA (commit) -> MMA, before TMEM is freed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  uint64_t* raw_full = bars + 18;  // [2] FP8 staging: TMA -> converter
+  uint64_t* raw_full = bars + 18;   // [2] FP8 staging: TMA -> converter warps
+  uint64_t* raw_empty = bars + 20;  // [2] FP8 staging: converter warps -> TMA
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -157,12 +152,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const uint32_t sbase = smem_u32(smem);
   if (threadIdx.x == 0) {
+    // FP8: a K/V tile is full when both converter warps have written their rows
+    const uint32_t fills = kFp8 ? kTcConvWarps : 1;
     for (int i = 0; i < kTcKStages; ++i) {
-      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_full[i]), fills);
       mbar_init(smem_u32(&k_empty[i]), 1);
     }
     for (int i = 0; i < kTcVStages; ++i) {
-      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_full[i]), fills);
       mbar_init(smem_u32(&v_empty[i]), 1);
     }
     for (int x = 0; x < kTcTiles; ++x) {
@@ -172,8 +169,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     mbar_init(smem_u32(mma_drain), 1);
     if (kFp8) {
-      mbar_init(smem_u32(&raw_full[0]), 1);
-      mbar_init(smem_u32(&raw_full[1]), 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(smem_u32(&raw_full[i]), 1);
+        mbar_init(smem_u32(&raw_empty[i]), kTcConvWarps);
+      }
     }
     mbar_init_fence();
   }
@@ -217,31 +216,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   bool ok = true;
 
+  // FP8 items in the 16-bit producer's order: K0, K1, then (V_m, K_{m+2}),
+  // then the last V tiles. Item i is TMA-loaded into staging slot i % 2 by
+  // the producer warp and converted into its fp16 K or V stage by warps 10-11.
+  const int k_first = min(2, n_total);
+  const int kv_pairs = max(0, n_total - 2);
+  auto item_at = [&](int i, bool& is_v, int& j) {
+    if (i < k_first) {
+      is_v = false;
+      j = i;
+    } else if (i - k_first < 2 * kv_pairs) {
+      const int m = i - k_first;
+      is_v = (m & 1) == 0;
+      j = is_v ? m / 2 : m / 2 + 2;
+    } else {
+      is_v = true;
+      j = kv_pairs + (i - k_first - 2 * kv_pairs);
+    }
+  };
+  const int n_items = 2 * n_total;
+
   if (warp == kTcProducerWarp && kFp8) {
-    // ------------------------------------------------ FP8 producer/converter --
-    // Items in the 16-bit producer's order: K0, K1, then (V_m, K_{m+2}), then
-    // the last V tiles. Item i is TMA-loaded into staging slot i % 2 one item
-    // ahead, then converted into its fp16 K or V stage.
+    // ------------------------------------------------------- FP8 producer --
     const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
     const int max_page_idx = (seq_len - 1) / p.block_size;
-    const int k0 = min(2, n_total);
-    const int pairs = max(0, n_total - 2);
-    auto item_at = [&](int i, bool& is_v, int& j) {
-      if (i < k0) {
-        is_v = false;
-        j = i;
-      } else if (i - k0 < 2 * pairs) {
-        const int m = i - k0;
-        is_v = (m & 1) == 0;
-        j = is_v ? m / 2 : m / 2 + 2;
-      } else {
-        is_v = true;
-        j = pairs + (i - k0 - 2 * pairs);
-      }
-    };
-    const int n_items = 2 * n_total;
     const uint32_t raw0 = sbase + L::kRaw0;
-    auto stage_raw = [&](int i) {  // TMA of item i into staging slot i % 2
+    int issued = 0;
+    for (int i = 0; i < n_items && ok; ++i) {
+      if (i >= 2) {  // slot i % 2 is free once both converters have read item i - 2
+        const bool got = mbar_wait(smem_u32(&raw_empty[i & 1]), ((i >> 1) - 1) & 1);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+      }
       bool is_v;
       int j;
       item_at(i, is_v, j);
@@ -262,72 +270,60 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_4d(raw0 + (i & 1) * kTcRawTileBytes + lane * kFp8TileBytes,
                     is_v ? &tmap_v : &tmap_k, bar, 0, kvh, row, page);
       }
-    };
-    int staged = 0, converted = 0;
-    if (n_items > 0) {
-      stage_raw(0);
-      staged = 1;
+      issued = i + 1;
     }
-    for (int i = 0; i < n_items && ok; ++i) {
+    if (!ok) {
+      if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+      for (int i = max(0, issued - 2); i < issued; ++i)  // loads still in flight
+        mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
+    }
+  } else if (kFp8 && warp >= kTcConvWarp0) {
+    // ----------------------------------------------- FP8 converter warps --
+    // Warp 10 converts rows 0-63 of every staged tile, warp 11 rows 64-127:
+    // chunk c of a row (E4M3 d = 16c .. 16c + 15) -> fp16 chunks 2c', 2c'+1
+    // of half c / 4 (c' = c % 4), all 128-byte swizzled like the TMA tiles.
+    const int row0 = (warp - kTcConvWarp0) * (kTcKv / kTcConvWarps);
+    const int c = lane & 7;
+    const int h = c >> 2;
+    const int c2 = (c & 3) * 2;
+    for (int i = 0; i < n_items; ++i) {
       bool is_v;
       int j;
       item_at(i, is_v, j);
       const int nst = is_v ? kTcVStages : kTcKStages;
       const int st = j % nst;
-      if (j >= nst) {  // the fp16 stage is free once the MMAs that read it retired
-        uint64_t* empty = is_v ? v_empty : k_empty;
-        const bool got = mbar_wait(smem_u32(&empty[st]), ((j / nst) - 1) & 1);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-      }
-      if (i + 1 < n_items) {  // slot (i+1) % 2 was converted last iteration
-        stage_raw(i + 1);
-        staged = i + 2;
-      }
-      const bool landed = mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
-      if (!__all_sync(0xffffffffu, landed)) {
+      bool got = true;
+      if (j >= nst)  // the fp16 stage is free once the MMAs that read it retired
+        got = mbar_wait(smem_u32(&(is_v ? v_empty : k_empty)[st]), ((j / nst) - 1) & 1);
+      if (got) got = mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
+      if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
-      converted = i + 1;
-      // 128 rows x 8 chunks of 16 E4M3 values; lane (r % 4, c) of each
-      // 4-row group: chunk c (d = 16c .. 16c + 15) -> fp16 chunks 2c', 2c'+1
-      // of half c / 4, both 128-byte swizzled like the TMA tiles
       const uint8_t* raw = smem + L::kRaw0 + (i & 1) * kTcRawTileBytes;
-      uint8_t* dst = smem + (is_v ? kTcV0 : kTcK0) + st * kTcTileBytes;
-      const int c = lane & 7;
-      const int h = c >> 2;
-      const int c2 = (c & 3) * 2;
+      uint8_t* dst = smem + (is_v ? kTcV0 : kTcK0) + st * kTcTileBytes + h * kTcHalf;
 #pragma unroll 4
-      for (int it = 0; it < kTcKv / 4; ++it) {
-        const int r = it * 4 + (lane >> 3);
+      for (int it = 0; it < kTcKv / kTcConvWarps / 4; ++it) {
+        const int r = row0 + it * 4 + (lane >> 3);
         const uint4 w = *reinterpret_cast<const uint4*>(raw + swz128(r, c));
         uint4 lo, hi;
-        lo.x = e4m3x2_f16x2(w.x);
-        lo.y = e4m3x2_f16x2(w.x >> 16);
-        lo.z = e4m3x2_f16x2(w.y);
-        lo.w = e4m3x2_f16x2(w.y >> 16);
-        hi.x = e4m3x2_f16x2(w.z);
-        hi.y = e4m3x2_f16x2(w.z >> 16);
-        hi.z = e4m3x2_f16x2(w.w);
-        hi.w = e4m3x2_f16x2(w.w >> 16);
-        uint8_t* drow = dst + h * kTcHalf;
-        *reinterpret_cast<uint4*>(drow + swz128(r, c2)) = lo;
-        *reinterpret_cast<uint4*>(drow + swz128(r, c2 + 1)) = hi;
+        e4m3x4_to_f16(w.x, lo.x, lo.y);
+        e4m3x4_to_f16(w.y, lo.z, lo.w);
+        e4m3x4_to_f16(w.z, hi.x, hi.y);
+        e4m3x4_to_f16(w.w, hi.z, hi.w);
+        *reinterpret_cast<uint4*>(dst + swz128(r, c2)) = lo;
+        *reinterpret_cast<uint4*>(dst + swz128(r, c2 + 1)) = hi;
       }
-      // generic-proxy writes (the fp16 tile) and reads (the staging slot,
-      // refilled by TMA next) -> async proxy, then hand the tile to the MMA
+      // generic-proxy reads of the staging slot (refilled by TMA) and writes
+      // of the fp16 tile (read by the MMAs) -> async proxy, then hand off
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(is_v ? &v_full[st] : &k_full[st]));
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&raw_empty[i & 1]));
+        mbar_arrive(smem_u32(is_v ? &v_full[st] : &k_full[st]));
+      }
     }
-    if (!ok) {
-      if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
-      for (int i = converted; i < staged; ++i)  // TMA loads still in flight
-        mbar_wait(smem_u32(&raw_full[i & 1]), (i >> 1) & 1);
-    }
+    if (!ok && lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
   } else if (warp == kTcProducerWarp) {
     // ------------------------------------------------------------ producer --
     // Issue order K0, K1, then (V_j, K_{j+2}) for j = 0, 1, ...: K runs two
@@ -620,7 +616,7 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   const int blocks = (max_q_len + tpc - 1) / tpc;
   if (blocks <= 0) return cudaSuccess;
   dim3 grid(blocks, num_kv_heads, num_seqs);
-  kernel<<<grid, kTcThreads, kSmem, stream>>>(mk, mv, p);
+  kernel<<<grid, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, p);
   return cudaGetLastError();
 }
 
