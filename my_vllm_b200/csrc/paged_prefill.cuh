@@ -25,6 +25,9 @@ struct PrefillParams {
   float scale_log2;  // softmax_scale * log2(e)
   const float* k_scale;  // FP8 caches: dequantisation scales (nullptr = 1)
   const float* v_scale;
+  int num_seqs;
+  int num_kv_heads;
+  int blocks_per_seq;  // row blocks of the longest query chunk
   int32_t* status;
 };
 

@@ -97,6 +97,99 @@ __device__ __forceinline__ uint32_t pair_to_f16(uint32_t w, __nv_bfloat16) {
   return Elem<__half>::pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
+// Work units are (sequence, row block, KV head). A unit's cost is the number
+// of 128-token KV tiles it streams, which grows with the sequence's cached
+// prefix and, under the causal mask, with the row block. The 1-D grid lists
+// the units longest first (ties by (sequence, row block) id, then KV head),
+// so the hardware's in-order block dispatch is greedy longest-processing-
+// time-first scheduling: without it, whole sequences with long prefixes can
+// land in the last wave. Every CTA recomputes the same order from the
+// metadata (no host sort, no workspace): a histogram of the (sequence,
+// row block) costs, the cost bucket holding its grid position, then the
+// position's rank inside that bucket in id order.
+constexpr int kTcCostKeys = 2048;  // cost keys are clamped here: order only, never results
+
+__device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int rb) {
+  const int q_len = __ldg(p.query_start_loc + s + 1) - __ldg(p.query_start_loc + s);
+  const int seq_len = __ldg(p.seq_lens + s);
+  const int tpc = (kTcTiles * kTcRows) / p.group;
+  const int tok_begin = rb * tpc;
+  if (tok_begin >= q_len || seq_len <= 0) return 0;
+  const int last_tok = min(q_len - 1, tok_begin + (min(kTcTiles * kTcRows, tpc * p.group) - 1) /
+                                                      p.group);
+  const int kv_limit = min(seq_len, max(1, seq_len - q_len + last_tok + 1));
+  return min((kv_limit + kTcKv - 1) / kTcKv, kTcCostKeys - 1);
+}
+
+// (sequence, row block, KV head) of grid position `pos`; `scratch` holds
+// kTcCostKeys + 2 ints of shared memory. Call with all threads of the CTA.
+__device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, int* scratch,
+                                               int& s, int& rb, int& kvh) {
+  int* hist = scratch;  // [kTcCostKeys]
+  const int pairs = p.num_seqs * p.blocks_per_seq;
+  for (int i = threadIdx.x; i < kTcCostKeys; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x)
+    atomicAdd(&hist[tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq)], 1);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int pair_pos = pos / p.num_kv_heads;
+    // bucket of pair_pos in descending cost order: lane l owns keys [64l, 64l+64)
+    constexpr int kPerLane = kTcCostKeys / 32;
+    int chunk = 0;
+    for (int k = 0; k < kPerLane; ++k) chunk += hist[lane * kPerLane + k];
+    int above = 0;  // pairs with larger keys: the chunks of lanes above this one
+    for (int l = 31; l > 0; --l) {
+      const int v = __shfl_sync(0xffffffffu, chunk, l);
+      if (l > lane) above += v;
+    }
+    int key = -1, rank = 0;
+    if (pair_pos >= above && pair_pos < above + chunk) {
+      int acc = above;
+      for (int k = kPerLane - 1; k >= 0; --k) {
+        const int h = hist[lane * kPerLane + k];
+        if (pair_pos < acc + h) {
+          key = lane * kPerLane + k;
+          rank = pair_pos - acc;
+          break;
+        }
+        acc += h;
+      }
+    }
+    const unsigned owner = __ballot_sync(0xffffffffu, key >= 0);
+    const int src = owner ? __ffs(owner) - 1 : 0;
+    key = __shfl_sync(0xffffffffu, key, src);
+    rank = __shfl_sync(0xffffffffu, rank, src);
+    // the rank-th pair (in id order) whose cost key is `key`
+    int found = 0;
+    for (int base = 0; base < pairs; base += 32) {
+      const int id = base + lane;
+      const bool hit = id < pairs &&
+                       tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq) == key;
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      const int n = __popc(m);
+      if (rank < n) {
+        unsigned mm = m;
+        for (int r = 0; r < rank; ++r) mm &= mm - 1;  // drop the lower set bits
+        found = base + __ffs(mm) - 1;
+        break;
+      }
+      rank -= n;
+    }
+    if (lane == 0) {
+      scratch[kTcCostKeys] = found;
+      scratch[kTcCostKeys + 1] = pos % p.num_kv_heads;
+    }
+  }
+  __syncthreads();
+  const int pair = scratch[kTcCostKeys];
+  kvh = scratch[kTcCostKeys + 1];
+  s = pair / p.blocks_per_seq;
+  rb = pair % p.blocks_per_seq;
+  __syncthreads();  // scratch is reused as the Q tiles
+}
+
 template <typename T, bool kFp8>
 __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -124,9 +217,8 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int s = blockIdx.z;
-  const int kvh = blockIdx.y;
-  const int rb = gridDim.x - 1 - blockIdx.x;  // heavier row blocks first
+  int s, rb, kvh;
+  tc_decode_unit(p, blockIdx.x, reinterpret_cast<int*>(smem + kTcQ), s, rb, kvh);
 
   const int q_start = p.query_start_loc[s];
   const int q_len = p.query_start_loc[s + 1] - q_start;
@@ -615,8 +707,13 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   const int tpc = (kTcTiles * kTcRows) / p.group;
   const int blocks = (max_q_len + tpc - 1) / tpc;
   if (blocks <= 0) return cudaSuccess;
-  dim3 grid(blocks, num_kv_heads, num_seqs);
-  kernel<<<grid, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, p);
+  PrefillParams q = p;
+  q.num_seqs = num_seqs;
+  q.num_kv_heads = num_kv_heads;
+  q.blocks_per_seq = blocks;
+  const int64_t units = (int64_t)blocks * num_kv_heads * num_seqs;
+  if (units > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, q);
   return cudaGetLastError();
 }
 

@@ -279,3 +279,21 @@ def test_full_decode_cuda_graph_replay(cuda_device):
         backend.check_status()
         assert_close_to_oracle(state.output[rows], expected, w.q.dtype)
     assert (state.output.float() - eager.float()).abs().max().item() <= MAX_ABS[w.q.dtype]
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 4), (32, 8), (8, 8)])
+def test_prefill_longest_first_order_covers_every_row(cuda_device, hq, hkv):
+    """The prefill grid lists (sequence, row block, KV head) units longest
+    first, decoded by every CTA from the metadata: every query row must be
+    written exactly as the oracle says (the output starts as NaN)."""
+    q_lens = [300, 1, 77, 513, 64, 190]
+    kv_lens = [300, 2000, 1077, 600, 64, 4000]
+    w = workloads.small_case(q_lens, kv_lens, len(q_lens), Hq=hq, Hkv=hkv, device=cuda_device)
+    out = torch.full_like(w.q, float("nan"))
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, w.query_start_loc,
+                      out, max(q_lens), 128 ** -0.5, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    expected, rows = sample_oracle(w, list(range(len(q_lens))))
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
