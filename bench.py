@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="smaller batches are for profiler captures only")
-    ap.add_argument("--workload", choices=("config2", "config3", "rope_append"),
+    ap.add_argument("--workload", choices=("config2", "config3", "config4", "rope_append"),
                     default="config2",
                     help="config3: mixed chunked prefill + decode (1 GPU), reports the "
                          "prefill kernel against the tensor roofline; rope_append: the "
@@ -654,6 +654,110 @@ def run_config3(args):
     print(json.dumps(line), flush=True)
 
 
+def run_config4(args, rank, world, local_rank):
+    """Config 4: Qwen3-32B heads sharded over ``world`` ranks (tp), all 64
+    layers' KV append + paged decode per step, B 512, context U[1024, 8192].
+    Each rank holds its own 64-layer cache shard in one allocation sized from
+    the free HBM; below tp 4 the pool cannot hold every block and the block
+    tables are sampled with replacement (stated in the line). value = KV +
+    append bytes of all ranks / max rank step time; tokens/s = 512 / step."""
+    from my_vllm_b200 import B200PagedBackend, ops, workloads
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+    if 8 % world:
+        raise SystemExit("--gpus must divide 8 KV heads")
+    free, _ = torch.cuda.mem_get_info(device)
+    layers = 64
+    w = workloads.config4_layers(device, tp=world, layers=layers,
+                                 memory_budget=max(0, free - (12 << 30)))
+    Hq, Hkv = 64 // world, 8 // world
+    backend = B200PagedBackend(Hq, Hkv, HEAD_DIM, BLOCK_SIZE, torch.bfloat16)
+    plan = backend.build_plan(w.common_metadata())
+    caches = [w.layer(l) for l in range(layers)]
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for kc, vc in caches:
+            ops.store_kvcache(w.key, w.value, kc, vc, w.slot_mapping)
+            backend.forward(w.q, w.key, w.value, kc, vc, plan)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = None
+    if rank == 0 and not args.no_clocks:
+        sampler = ClockSampler(physical_gpu_indices(world))
+        sampler.start()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    wall0 = time.time()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    wall1 = time.time()
+    barrier()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    backend.check_status()
+    if sampler is not None:
+        sampler.mark(wall0, wall1)
+        sampler.stop()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    per_rank = (w.kv_bytes_read_per_layer() + w.append_bytes_per_layer()) * layers
+    total = per_rank * world
+    hbm, src = peaks()
+    per_gpu = per_rank / (ms * 1e-3) / 1e9
+    n_parts = plan.metadata.decode_plan.num_parts
+    line = {
+        "metric": METRIC + " (config 4, 64 layers)", "value": round(total / (ms * 1e-3) / 1e9, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "tokens_per_s": round(512 / (ms * 1e-3), 1),
+        "config": {"workload": "config4: Qwen3-32B heads (64 q / 8 KV, D 128), 64 layers of KV "
+                               "append + paged decode per step, B 512, ctx U[1024, 8192], bs 16",
+                   "parallelism": f"tp{world}: KV heads sharded, {Hq} q / {Hkv} KV heads per "
+                                  "rank, no data-path collective",
+                   "pool_blocks_per_layer": w.pool_blocks,
+                   "block_tables": "sampled with replacement (pool smaller than the batch needs)"
+                                   if w.with_replacement else "seeded permutation",
+                   "decode_split": n_parts,
+                   "l2": f"{per_rank / 1e9:.1f} GB of paged KV per rank per step"},
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel + kv_append_kernel",
+                     "achieved": round(per_gpu, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(per_gpu / hbm, 4), "peak_source": src},
+        "gpu_launches": layers * (2 + (1 if n_parts > 1 else 0)) * args.steps,
+    }
+    if sampler is not None:
+        line["clocks"] = sampler.summary()
+    print(json.dumps(line), flush=True)
+
+
 def run_rope_append(args):
     """The step before attention, fused: q/k RMSNorm + neox RoPE + KV append
     for one layer of Qwen3-8B (Hq 32, Hkv 8, D 128) over --rope-tokens new
@@ -766,6 +870,11 @@ def main():
         return
     if args.workload == "rope_append":
         run_rope_append(args)
+        return
+    if args.workload == "config4":
+        if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+        run_config4(args, rank, int(os.environ.get("WORLD_SIZE", "1")), local_rank)
         return
     if world != args.gpus and "WORLD_SIZE" not in os.environ:
         world = args.gpus

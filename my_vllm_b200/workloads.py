@@ -257,6 +257,95 @@ def small_case(query_lengths, kv_lengths, num_prefill, *, Hq=16, Hkv=4, D=128, b
     return w
 
 
+@dataclass
+class LayeredDecode:
+    """Config 4 for one tensor-parallel rank: every layer's paged cache as
+    views of one ``[2, L, N, bs, Hkv, D]`` allocation (ModelRunner.allocate_kv_cache,
+    nanovllm/engine/model_runner.py:325-352), one block table shared by all
+    layers, and one decode batch."""
+
+    kv_cache: torch.Tensor
+    q: torch.Tensor
+    key: torch.Tensor
+    value: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor
+    seq_lens: torch.Tensor
+    query_start_loc: torch.Tensor
+    seq_lens_host: list
+    block_counts: tuple
+    pool_blocks: int
+    with_replacement: bool
+
+    @property
+    def num_layers(self) -> int:
+        return self.kv_cache.size(1)
+
+    def layer(self, i: int):
+        return self.kv_cache[0, i], self.kv_cache[1, i]
+
+    def common_metadata(self):
+        B = len(self.seq_lens_host)
+        return CommonAttentionMetadata(
+            num_prefill_seqs=0, num_decode_seqs=B, num_prefill_tokens=0, num_decode_tokens=B,
+            query_start_loc=self.query_start_loc, seq_lens=self.seq_lens,
+            slot_mapping=self.slot_mapping, block_tables=self.block_tables, max_q_len=1,
+            max_kv_len=max(self.seq_lens_host), block_counts=self.block_counts,
+            num_kv_blocks=sum(self.block_counts), trusted=True)
+
+    def kv_bytes_read_per_layer(self) -> int:
+        per_token = self.kv_cache.size(4) * self.kv_cache.size(5) * self.kv_cache.element_size() * 2
+        return sum(self.seq_lens_host) * per_token
+
+    def append_bytes_per_layer(self) -> int:
+        row = self.kv_cache.size(4) * self.kv_cache.size(5) * self.kv_cache.element_size() * 2
+        return len(self.seq_lens_host) * row
+
+
+def config4_layers(device, *, tp=8, batch=512, layers=64, seed=SEED_BASE + 4,
+                   memory_budget=None, dtype=torch.bfloat16) -> LayeredDecode:
+    """Qwen3-32B tensor-parallel decode, all layers of one rank: Hq 64/tp,
+    Hkv 8/tp, B 512, context U[1024, 8192], bs 16. The per-layer pool holds
+    every block the batch needs when ``memory_budget`` bytes allow (tp >= 4
+    on a 180 GB B200); otherwise it is as large as the budget allows and the
+    block tables are sampled with replacement (HBM traffic is unchanged: the
+    footprint is far beyond L2)."""
+    device = torch.device(device)
+    Hq, Hkv, D, bs = 64 // tp, 8 // tp, 128, 16
+    g = _generator(seed, torch.device("cpu"))
+    ctx = torch.randint(1024, 8193, (batch,), generator=g).tolist()
+    counts = [(c + bs - 1) // bs for c in ctx]
+    need = sum(counts)
+    block_bytes = bs * Hkv * D * torch.tensor([], dtype=dtype).element_size()
+    if memory_budget is None:
+        memory_budget = need * block_bytes * 2 * layers
+    pool = max(1, min(need, int(memory_budget // (block_bytes * 2 * layers))))
+    replace = pool < need
+    picks = (torch.randint(0, pool, (need,), generator=g) if replace
+             else torch.randperm(pool, generator=g)[:need]).tolist()
+    width = max(counts)
+    table = torch.full((batch, width), -1, dtype=torch.int32)
+    slots, cursor = [], 0
+    for i, n in enumerate(counts):
+        row = picks[cursor: cursor + n]
+        cursor += n
+        table[i, :n] = torch.tensor(row, dtype=torch.int32)
+        slots.append(row[(ctx[i] - 1) // bs] * bs + (ctx[i] - 1) % bs)
+    kv = torch.empty((2, layers, pool, bs, Hkv, D), dtype=dtype, device=device)
+    gen = _generator(seed, device)
+    for i in range(2):
+        for l in range(layers):
+            kv[i, l].copy_(_randn(kv[i, l].shape, gen, device, dtype))
+    return LayeredDecode(
+        kv_cache=kv, q=_randn((batch, Hq, D), gen, device, dtype),
+        key=_randn((batch, Hkv, D), gen, device, dtype),
+        value=_randn((batch, Hkv, D), gen, device, dtype),
+        slot_mapping=torch.tensor(slots, dtype=torch.int32, device=device),
+        block_tables=table.to(device), seq_lens=torch.tensor(ctx, dtype=torch.int32, device=device),
+        query_start_loc=torch.arange(batch + 1, dtype=torch.int32, device=device),
+        seq_lens_host=ctx, block_counts=tuple(counts), pool_blocks=pool, with_replacement=replace)
+
+
 def ragged_decode(device="cuda", dtype=torch.bfloat16, seed=SEED_BASE + 6, *, batch=40,
                   ctx=(1, 6000), num_q_heads=32, num_kv_heads=8) -> Workload:
     """A decode batch with context lengths U[ctx], bs 16, permuted pool."""
