@@ -58,6 +58,10 @@ def parse_args():
     ap.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
                     help="fp8: the config 2 step over an FP8 E4M3 KV pool (scales 1.0); "
                          "bytes are counted at one byte per element")
+    ap.add_argument("--comparator", choices=("none", "flashinfer"), default="none",
+                    help="flashinfer: also time the library decode the reference engine calls "
+                         "(BatchDecodeWithPagedKVCacheWrapper, configured as "
+                         "FlashInferBackend does) on the same config 2 inputs; one extra line")
     ap.add_argument("--rope-tokens", type=int, default=16384,
                     help="tokens per rope_append step (a long prefill chunk)")
     return ap.parse_args()
@@ -654,6 +658,112 @@ def run_config3(args):
     print(json.dumps(line), flush=True)
 
 
+def run_flashinfer_comparator(args):
+    """Config 2 decode through FlashInfer's paged decode wrapper, set up the
+    way the reference's FlashInferBackend sets it up (NHD, backend "auto",
+    bf16 q/kv/o, CSR page indices from the block tables,
+    nanovllm/layers/attention_backend.py:544-548, 726-758, 827-839), timed
+    with CUDA events on the same inputs as our decode kernel, plus the
+    max-abs difference between the two outputs."""
+    import flashinfer
+
+    from my_vllm_b200 import B200PagedBackend, workloads
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    w = workloads.config2(device=device, batch=args.batch)
+    B, bs = w.num_seqs, w.block_size
+    counts = torch.tensor(w.block_counts, dtype=torch.int32, device=device)
+    indptr = torch.zeros(B + 1, dtype=torch.int32, device=device)
+    indptr[1:] = torch.cumsum(counts, 0)
+    width = w.block_tables.size(1)
+    mask = torch.arange(width, device=device)[None, :] < counts[:, None]
+    indices = w.block_tables[mask].contiguous()
+    last = ((w.seq_lens - 1) % bs + 1).to(torch.int32)
+    workspace = torch.zeros(128 << 20, dtype=torch.uint8, device=device)
+    wrapper = flashinfer.BatchDecodeWithPagedKVCacheWrapper(workspace, kv_layout="NHD",
+                                                            backend="auto")
+    wrapper.plan(indptr, indices, last, w.num_q_heads, w.num_kv_heads, HEAD_DIM, bs,
+                 pos_encoding_mode="NONE", q_data_type=torch.bfloat16,
+                 kv_data_type=torch.bfloat16, o_data_type=torch.bfloat16)
+    out_fi = torch.empty_like(w.q)
+    stream = torch.cuda.current_stream(device)
+
+    def fi():
+        wrapper.run(w.q, (w.k_cache, w.v_cache), out=out_fi)
+
+    backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, bs, torch.bfloat16)
+    plan = backend.build_plan(w.common_metadata())
+
+    def ours():
+        return backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    fi_ms = timed(fi)
+    our_ms = timed(ours)
+    diff = float((ours().float() - out_fi.float()).abs().max())
+    kv = w.kv_bytes_read()
+
+    # config 3's prefill part through the prefill wrapper (causal, NHD)
+    w3 = workloads.config3(device=device)
+    nP = w3.num_prefill_seqs
+    P = int(w3.extra["qsl_host"][nP])
+    counts3 = torch.tensor(w3.block_counts[:nP], dtype=torch.int32, device=device)
+    kv_indptr3 = torch.zeros(nP + 1, dtype=torch.int32, device=device)
+    kv_indptr3[1:] = torch.cumsum(counts3, 0)
+    mask3 = torch.arange(w3.block_tables.size(1), device=device)[None, :] < counts3[:, None]
+    indices3 = w3.block_tables[:nP][mask3].contiguous()
+    last3 = ((w3.seq_lens[:nP] - 1) % bs + 1).to(torch.int32)
+    pwrap = flashinfer.BatchPrefillWithPagedKVCacheWrapper(workspace, kv_layout="NHD",
+                                                           backend="auto")
+    pwrap.plan(w3.query_start_loc[: nP + 1], kv_indptr3, indices3, last3, 32, 8, HEAD_DIM, bs,
+               causal=True, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+               o_data_type=torch.bfloat16)
+    out3_fi = torch.empty_like(w3.q[:P])
+    out3 = torch.empty_like(w3.q[:P])
+    from my_vllm_b200 import ops
+
+    def fi_prefill():
+        pwrap.run(w3.q[:P], (w3.k_cache, w3.v_cache), out=out3_fi)
+
+    def our_prefill():
+        ops.paged_prefill(w3.q[:P], w3.k_cache, w3.v_cache, w3.block_tables[:nP],
+                          w3.seq_lens[:nP], w3.query_start_loc[: nP + 1], out3, 512,
+                          HEAD_DIM ** -0.5, num_seqs=nP)
+
+    fi_pre_ms = timed(fi_prefill)
+    our_pre_ms = timed(our_prefill)
+    pre_diff = float((out3.float() - out3_fi.float()).abs().max())
+    line = {
+        "impl": "flashinfer-comparator", "metric": "paged decode HBM GB/s (decode launch only)",
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config2 decode, B {B}, ctx {CONTEXT}, Hq 32 / Hkv 8, bs 16",
+                   "flashinfer": flashinfer.__version__,
+                   "wrapper": "BatchDecodeWithPagedKVCacheWrapper(NHD, backend=auto)"},
+        "flashinfer_ms": round(fi_ms, 5), "flashinfer_gbs": round(kv / (fi_ms * 1e-3) / 1e9, 1),
+        "ours_ms": round(our_ms, 5), "ours_gbs": round(kv / (our_ms * 1e-3) / 1e9, 1),
+        "speedup": round(fi_ms / our_ms, 3), "max_abs_diff": diff,
+        "prefill_config3": {"flashinfer_ms": round(fi_pre_ms, 5), "ours_ms": round(our_pre_ms, 5),
+                            "speedup": round(fi_pre_ms / our_pre_ms, 3),
+                            "max_abs_diff": pre_diff,
+                            "wrapper": "BatchPrefillWithPagedKVCacheWrapper(NHD, backend=auto, "
+                                       "causal)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_config4(args, rank, world, local_rank):
     """Config 4: Qwen3-32B heads sharded over ``world`` ranks (tp), all 64
     layers' KV append + paged decode per step, B 512, context U[1024, 8192].
@@ -864,6 +974,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.comparator == "flashinfer":
+        run_flashinfer_comparator(args)
         return
     if args.workload == "config3":
         run_config3(args)
