@@ -893,13 +893,20 @@ def run_rope_append(args):
     qw = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
     kw = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
     num_blocks = max(2 * T // BLOCK_SIZE, 1)
-    k_cache = torch.zeros(num_blocks, BLOCK_SIZE, Hkv, D, dtype=torch.bfloat16, device=device)
+    fp8 = args.kv_dtype == "fp8"
+    k_cache = torch.zeros(num_blocks, BLOCK_SIZE, Hkv, D,
+                          dtype=torch.float8_e4m3fn if fp8 else torch.bfloat16, device=device)
     v_cache = torch.zeros_like(k_cache)
+    if fp8:
+        ops.register_kv_scales(k_cache, v_cache, torch.ones(1, device=device),
+                               torch.ones(1, device=device))
     slots = torch.randperm(num_blocks * BLOCK_SIZE, generator=g, device=device)[:T].to(torch.int32)
     q_out = torch.empty_like(q)
     stream = torch.cuda.current_stream(device)
     es = 2
-    alg_bytes = (T * (Hq + 2 * Hkv) * D * es) * 2 + T * D * 4
+    # reads: q, k, v rows + one cos|sin row; writes: rotated q + the k/v cache rows
+    alg_bytes = (T * (Hq + 2 * Hkv) * D * es) + T * D * 4 + T * Hq * D * es + \
+        T * 2 * Hkv * D * k_cache.element_size()
 
     def fused():
         ops.qk_norm_rope_append(q, k, v, positions, qw, kw, table, 1e-6, k_cache, v_cache,
@@ -919,7 +926,7 @@ def run_rope_append(args):
 
         qr = rope(norm(q, qw))
         kr = rope(norm(k, kw))
-        ops.store_kvcache(kr, v, k_cache, v_cache, slots)
+        ops.store_kvcache(kr, v, k_cache, v_cache, slots)  # FP8 pools quantise here
         return qr
 
     def timed(fn, steps):
@@ -950,7 +957,8 @@ def run_rope_append(args):
         "metric": "fused q/k-norm + RoPE + KV append HBM GB/s", "value": round(gbs, 1),
         "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "bf16 (KV cache fp8-e4m3)" if fp8 else "bf16",
+        "data": "synthetic",
         "tokens_per_s": round(T / (ms * 1e-3), 1),
         "config": {"workload": f"rope_append: {T} new tokens of Qwen3-8B (Hq 32, Hkv 8, D 128), "
                                "positions U[0, 40960), rope theta 1e6, bs 16, random slots",

@@ -89,9 +89,11 @@ B200_API int b200_store_kvcache(const void* key, int64_t key_row_stride,
 /*
  * KV append into an FP8 E4M3 cache (see b200_paged_cache.kv_fp8). No
  * counterpart in the reference. For every token i with a slot s != -1:
- *   k_cache[s][e] = fp8(key[i][e] / *k_scale), v_cache[s][e] = fp8(value[i][e] / *v_scale)
- * for e < row_elems, where x / scale is the IEEE fp32 quotient (scale NULL = 1)
- * and fp8() rounds to nearest even, saturating to +-448 (NaN stays NaN).
+ *   k_cache[s][e] = fp8(key[i][e] * rk), v_cache[s][e] = fp8(value[i][e] * rv)
+ * for e < row_elems, where rk = 1 / *k_scale and rv = 1 / *v_scale are
+ * correctly rounded to fp32 once (scale NULL = 1), each product is one fp32
+ * multiply, and fp8() rounds to nearest even, saturating to +-448 (NaN
+ * stays NaN).
  * key/value: 16-bit rows of `src_dtype` with row strides in elements;
  * caches: one byte per element, cache_slot_stride bytes between slots.
  * row_elems must be a multiple of 16; rows, strides and caches 16-byte
@@ -133,6 +135,23 @@ B200_API int b200_qk_norm_rope_append(
     int64_t max_position, void* k_cache, void* v_cache, int64_t cache_slot_stride,
     const int32_t* slot_mapping, int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
     int32_t head_dim, int32_t dtype, int64_t num_slots, int32_t* status, void* stream);
+
+/*
+ * The same fused step into an FP8 E4M3 pool (see b200_paged_cache.kv_fp8).
+ * No counterpart in the reference. q_out is produced as above; the rotated k
+ * row, rounded to `dtype`, and the v row are quantised exactly as
+ * b200_store_kvcache_fp8 quantises 16-bit rows (scales NULL = 1). k_cache / v_cache hold one byte per
+ * element and cache_slot_stride counts bytes (a multiple of 16).
+ */
+B200_API int b200_qk_norm_rope_append_fp8(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+    int64_t k_token_stride, const void* v, int64_t v_token_stride, void* q_out,
+    int64_t q_out_token_stride, int64_t q_out_head_stride, const void* q_weight,
+    const void* k_weight, float eps, const int64_t* positions, const float* cos_sin_cache,
+    int64_t max_position, void* k_cache, void* v_cache, int64_t cache_slot_stride,
+    const int32_t* slot_mapping, int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype, const float* k_scale, const float* v_scale,
+    int64_t num_slots, int32_t* status, void* stream);
 
 /*
  * Slot mapping of the new tokens, built on the device. Replaces the host loop

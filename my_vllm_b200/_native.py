@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "b200_store_kvcache_fp8",
     "b200_build_slot_mapping",
     "b200_qk_norm_rope_append",
+    "b200_qk_norm_rope_append_fp8",
     "b200_paged_decode_plan",
     "b200_paged_decode",
     "b200_paged_prefill",
@@ -104,6 +105,13 @@ _SIGNATURES = {
         [
             _VP, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _F32, _VP, _VP,
             _I64, _VP, _VP, _I64, _VP, _I64, _I32, _I32, _I32, _I32, _I64, _VP, _VP,
+        ],
+        _I32,
+    ),
+    "b200_qk_norm_rope_append_fp8": (
+        [
+            _VP, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _F32, _VP, _VP,
+            _I64, _VP, _VP, _I64, _VP, _I64, _I32, _I32, _I32, _I32, _VP, _VP, _I64, _VP, _VP,
         ],
         _I32,
     ),

@@ -211,7 +211,12 @@ int b200_store_kvcache(const void* key, int64_t key_row_stride, const void* valu
   return B200_OK;
 }
 
-int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head_stride,
+}  // extern "C"
+
+namespace {
+// Shared by b200_qk_norm_rope_append and its FP8-cache variant (fp8: caches
+// hold one byte per element; cache_slot_stride counts bytes then).
+int rope_append_impl(const void* q, int64_t q_token_stride, int64_t q_head_stride,
                              const void* k, int64_t k_token_stride, const void* v,
                              int64_t v_token_stride, void* q_out, int64_t q_out_token_stride,
                              int64_t q_out_head_stride, const void* q_weight,
@@ -220,7 +225,8 @@ int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_he
                              void* v_cache, int64_t cache_slot_stride,
                              const int32_t* slot_mapping, int64_t num_tokens,
                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                             int32_t dtype, int64_t num_slots, int32_t* status, void* stream) {
+                             int32_t dtype, int64_t num_slots, bool fp8, const float* k_scale,
+                             const float* v_scale, int32_t* status, void* stream) {
   g_last_error.clear();
   if (head_dim != b200::kRopeHeadDim) return fail(B200_ERR_UNSUPPORTED, "head_dim must be 128");
   if (dtype != B200_DTYPE_BFLOAT16 && dtype != B200_DTYPE_FLOAT16)
@@ -268,10 +274,52 @@ int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_he
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
   p.num_slots = num_slots;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
   p.status = status;
-  cudaError_t e = b200::launch_qk_norm_rope_append(p, dtype, static_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      b200::launch_qk_norm_rope_append(p, dtype, fp8, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "q/k norm + rope + append launch");
   return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head_stride,
+                             const void* k, int64_t k_token_stride, const void* v,
+                             int64_t v_token_stride, void* q_out, int64_t q_out_token_stride,
+                             int64_t q_out_head_stride, const void* q_weight,
+                             const void* k_weight, float eps, const int64_t* positions,
+                             const float* cos_sin_cache, int64_t max_position, void* k_cache,
+                             void* v_cache, int64_t cache_slot_stride,
+                             const int32_t* slot_mapping, int64_t num_tokens,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t dtype, int64_t num_slots, int32_t* status, void* stream) {
+  return rope_append_impl(q, q_token_stride, q_head_stride, k, k_token_stride, v, v_token_stride,
+                          q_out, q_out_token_stride, q_out_head_stride, q_weight, k_weight, eps,
+                          positions, cos_sin_cache, max_position, k_cache, v_cache,
+                          cache_slot_stride, slot_mapping, num_tokens, num_q_heads,
+                          num_kv_heads, head_dim, dtype, num_slots, false, nullptr, nullptr,
+                          status, stream);
+}
+
+int b200_qk_norm_rope_append_fp8(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+    int64_t k_token_stride, const void* v, int64_t v_token_stride, void* q_out,
+    int64_t q_out_token_stride, int64_t q_out_head_stride, const void* q_weight,
+    const void* k_weight, float eps, const int64_t* positions, const float* cos_sin_cache,
+    int64_t max_position, void* k_cache, void* v_cache, int64_t cache_slot_stride,
+    const int32_t* slot_mapping, int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype, const float* k_scale, const float* v_scale,
+    int64_t num_slots, int32_t* status, void* stream) {
+  return rope_append_impl(q, q_token_stride, q_head_stride, k, k_token_stride, v, v_token_stride,
+                          q_out, q_out_token_stride, q_out_head_stride, q_weight, k_weight, eps,
+                          positions, cos_sin_cache, max_position, k_cache, v_cache,
+                          cache_slot_stride, slot_mapping, num_tokens, num_q_heads,
+                          num_kv_heads, head_dim, dtype, num_slots, true, k_scale, v_scale,
+                          status, stream);
 }
 
 int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride,

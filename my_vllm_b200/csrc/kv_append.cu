@@ -132,7 +132,8 @@ cudaError_t launch_kv_append(const void* key, int64_t key_row_stride,
 
 // Append into an FP8 E4M3 cache: each thread quantises 16 consecutive
 // elements of one K or V row (two 16-byte loads, one 16-byte store):
-// stored = e4m3(x / scale), IEEE quotient, round to nearest even with
+// stored = e4m3(x * inv), inv = 1 / scale rounded once to fp32 (one multiply
+// per element instead of a division), round to nearest even with
 // saturation to +-448 (cvt.rn.satfinite; NaN stays NaN).
 template <typename T>
 __device__ __forceinline__ float2 widen2(uint32_t w);
@@ -160,8 +161,9 @@ __global__ void __launch_bounds__(256)
                          int64_t cache_slot_stride, const int32_t* __restrict__ slot_mapping,
                          int64_t num_tokens, int64_t vecs_per_row, const float* k_scale,
                          const float* v_scale, int64_t num_slots, int32_t* status) {
-  const float ks = k_scale != nullptr ? __ldg(k_scale) : 1.f;
-  const float vs = v_scale != nullptr ? __ldg(v_scale) : 1.f;
+  // reciprocals of the dequantisation scales, correctly rounded to fp32
+  const float ks = __frcp_rn(k_scale != nullptr ? __ldg(k_scale) : 1.f);
+  const float vs = __frcp_rn(v_scale != nullptr ? __ldg(v_scale) : 1.f);
   const int64_t per_token = 2 * vecs_per_row;
   const int64_t total = num_tokens * per_token;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -186,8 +188,8 @@ __global__ void __launch_bounds__(256)
     for (int i = 0; i < 4; ++i) {
       const float2 x0 = widen2<T>(w[2 * i]);
       const float2 x1 = widen2<T>(w[2 * i + 1]);
-      const uint32_t lo = e4m3x2(__fdiv_rn(x0.x, sc), __fdiv_rn(x0.y, sc));
-      const uint32_t hi = e4m3x2(__fdiv_rn(x1.x, sc), __fdiv_rn(x1.y, sc));
+      const uint32_t lo = e4m3x2(__fmul_rn(x0.x, sc), __fmul_rn(x0.y, sc));
+      const uint32_t hi = e4m3x2(__fmul_rn(x1.x, sc), __fmul_rn(x1.y, sc));
       out[i] = lo | (hi << 16);
     }
     *reinterpret_cast<uint4*>((is_v ? v_cache : k_cache) + slot * cache_slot_stride + vec * 16) =

@@ -8,12 +8,16 @@
 //   q rows: normalise, scale by q_weight, rotate -> q_out
 //   k rows: normalise, scale by k_weight, rotate -> k_cache[slot]
 //   v rows: copied to v_cache[slot]
-// so the rotated k never exists outside the cache. Rounding follows the
+// so the rotated k never exists outside the cache. With an FP8 E4M3 pool the
+// k and v rows are quantised on the way in, exactly as the FP8 append would
+// quantise the 16-bit rows (k after its rounding to the 16-bit type). Rounding follows the
 // reference's eager math: the normalised row is rounded to the 16-bit type,
 // multiplied by the 16-bit weight and rounded again, then rotated in fp32 from
 // those values (no fused multiply-adds, IEEE square root and division) and
 // rounded once more.
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "rope_append.cuh"
@@ -104,10 +108,39 @@ __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
 // every warp keeps 4 KiB of loads in flight.
 constexpr int kRowsInFlight = 4;  // rows each lane group loads before computing
 
+// FP8 E4M3 cache rows: 8 values of T (4 words) -> 8 bytes, each
+// e4m3(x * inv) with inv = 1 / scale rounded once to fp32, round to nearest even and
+// saturation to +-448 (the semantics of b200_store_kvcache_fp8).
 template <typename T>
+__device__ __forceinline__ uint2 quantize8(const uint32_t (&w)[4], float inv) {
+  uint32_t out[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float lo, hi;
+      f2_split(Pair<T>::widen(w[2 * h + i]), lo, hi);
+      uint16_t r;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
+          : "=h"(r)
+          : "f"(__fmul_rn(hi, inv)), "f"(__fmul_rn(lo, inv)));
+      bytes |= static_cast<uint32_t>(r) << (16 * i);
+    }
+    out[h] = bytes;
+  }
+  return make_uint2(out[0], out[1]);
+}
+
+template <typename T, bool kFp8>
 __global__ void __launch_bounds__(256, 2)
     qk_norm_rope_append_kernel(const RopeAppendParams p) {
   using P = Pair<T>;
+  // cache element type: T, or one byte (E4M3) per element
+  using C = typename std::conditional<kFp8, uint8_t, T>::type;
+  // FP8: reciprocals of the dequantisation scales, correctly rounded to fp32
+  const float k_inv = __frcp_rn(kFp8 && p.k_scale != nullptr ? __ldg(p.k_scale) : 1.f);
+  const float v_inv = __frcp_rn(kFp8 && p.v_scale != nullptr ? __ldg(p.v_scale) : 1.f);
   __shared__ uint4 weights[2][16];  // q_weight, k_weight
   if (threadIdx.x < 32)
     weights[threadIdx.x >> 4][threadIdx.x & 15] = __ldg(
@@ -174,12 +207,18 @@ __global__ void __launch_bounds__(256, 2)
       for (int u = 0; u < kRowsInFlight; ++u) {
         if (!src[u]) continue;
         const int j = j0 + 4 * u;
-        if (j >= hqk) {  // v row: copied into the cache slot unchanged
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) +
-                                                (int64_t)slot * p.cache_slot_stride +
-                                                (j - hqk) * kRopeHeadDim);
-          dst[l] = a[u];
-          dst[8 + l] = b[u];
+        if (j >= hqk) {  // v row: copied (or quantised) into the cache slot
+          C* dst = reinterpret_cast<C*>(p.v_cache) + (int64_t)slot * p.cache_slot_stride +
+                   (j - hqk) * kRopeHeadDim;
+          if constexpr (kFp8) {
+            const uint32_t wa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+            const uint32_t wb[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+            reinterpret_cast<uint2*>(dst)[l] = quantize8<T>(wa, v_inv);
+            reinterpret_cast<uint2*>(dst)[8 + l] = quantize8<T>(wb, v_inv);
+          } else {
+            reinterpret_cast<uint4*>(dst)[l] = a[u];
+            reinterpret_cast<uint4*>(dst)[8 + l] = b[u];
+          }
           continue;
         }
         const bool is_q = j < hq;
@@ -216,6 +255,14 @@ __global__ void __launch_bounds__(256, 2)
           y1w[i] = P::narrow(f2_sub(f2_mul(n1, cs[i]), f2_mul(n2, sn[i])));
           y2w[i] = P::narrow(f2_add(f2_mul(n2, cs[i]), f2_mul(n1, sn[i])));
         }
+        if (kFp8 && !is_q) {  // rotated k, rounded to T, then quantised like the append
+          uint2* dst = reinterpret_cast<uint2*>(reinterpret_cast<C*>(p.k_cache) +
+                                                (int64_t)slot * p.cache_slot_stride +
+                                                (j - hq) * kRopeHeadDim);
+          dst[l] = quantize8<T>(y1w, k_inv);
+          dst[8 + l] = quantize8<T>(y2w, k_inv);
+          continue;
+        }
         uint4* dst = reinterpret_cast<uint4*>(
             is_q ? reinterpret_cast<T*>(p.q_out) + t * p.q_out_token_stride +
                        j * p.q_out_head_stride
@@ -228,17 +275,24 @@ __global__ void __launch_bounds__(256, 2)
   }
 }
 
-cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype,
+cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype, bool fp8_cache,
                                        cudaStream_t stream) {
   // 8 warps per block, one token per warp; at most the 2 blocks per SM that
   // fit at once, the grid-stride loop covers the rest
   int64_t blocks = (p.num_tokens + 7) / 8;
   if (blocks > 148 * 2) blocks = 148 * 2;
   if (blocks < 1) blocks = 1;
-  if (dtype == B200_DTYPE_BFLOAT16)
-    qk_norm_rope_append_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(p);
-  else
-    qk_norm_rope_append_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(p);
+  if (dtype == B200_DTYPE_BFLOAT16) {
+    if (fp8_cache)
+      qk_norm_rope_append_kernel<__nv_bfloat16, true><<<(unsigned)blocks, 256, 0, stream>>>(p);
+    else
+      qk_norm_rope_append_kernel<__nv_bfloat16, false><<<(unsigned)blocks, 256, 0, stream>>>(p);
+  } else {
+    if (fp8_cache)
+      qk_norm_rope_append_kernel<__half, true><<<(unsigned)blocks, 256, 0, stream>>>(p);
+    else
+      qk_norm_rope_append_kernel<__half, false><<<(unsigned)blocks, 256, 0, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 

@@ -27,16 +27,18 @@ struct RopeAppendParams {
   int64_t max_position;
   void* k_cache;
   void* v_cache;
-  int64_t cache_slot_stride;    // elements between consecutive slots (Hkv * 128)
+  int64_t cache_slot_stride;    // cache elements between consecutive slots (Hkv * 128)
   const int32_t* slot_mapping;  // [T], -1 = no cache write
   int64_t num_tokens;
   int num_q_heads;
   int num_kv_heads;
   int64_t num_slots;
+  const float* k_scale;  // FP8 caches: quantisation scales (nullptr = 1)
+  const float* v_scale;
   int32_t* status;
 };
 
-cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype,
+cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype, bool fp8_cache,
                                        cudaStream_t stream);
 
 }  // namespace b200

@@ -125,8 +125,8 @@ def store_kvcache_fp8(
     *,
     status: torch.Tensor | None = None,
 ) -> None:
-    """Quantise K/V rows into FP8 E4M3 cache slots: ``cache = e4m3(x / scale)``
-    (IEEE quotient, round to nearest even, saturate to +-448); slots of -1
+    """Quantise K/V rows into FP8 E4M3 cache slots: ``cache = e4m3(x * (1/scale))``
+    (reciprocal rounded once to fp32, round to nearest even, saturate to +-448); slots of -1
     are skipped. The FP8 counterpart of ``store_kvcache``; ``k_scale`` and
     ``v_scale`` are 1-element float32 CUDA tensors (None = 1)."""
     N, num_heads, head_dim = key.shape
@@ -186,6 +186,9 @@ def qk_norm_rope_append(
     (into ``q_out``, which may be ``q`` itself) and writes the rotated k and
     the v rows into their cache slots. ``cos_sin_cache`` is the engine's
     fp32 table ([max_position, 128] or [max_position, 1, 128]: cos | sin).
+    An FP8 pool (``torch.float8_e4m3fn`` caches) receives k and v quantised
+    with the scales ``register_kv_scales`` attached, as ``store_kvcache_fp8``
+    would store the 16-bit rows.
     """
     T, Hq, D = q.shape
     Hkv = k.shape[1]
@@ -196,8 +199,9 @@ def qk_norm_rope_append(
         _require_cuda(name, t)
     if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("q, k and v must share one float16/bfloat16 dtype")
-    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
-        raise TypeError("caches must have the q dtype")
+    fp8 = k_cache.dtype == FP8_DTYPE
+    if (k_cache.dtype != q.dtype and not fp8) or v_cache.dtype != k_cache.dtype:
+        raise TypeError("caches must have the q dtype, or both be torch.float8_e4m3fn")
     if q_weight.dtype != q.dtype or k_weight.dtype != q.dtype:
         raise TypeError("norm weights must have the q dtype")
     if positions.dtype != torch.int64 or slot_mapping.dtype != torch.int32:
@@ -221,14 +225,21 @@ def qk_norm_rope_append(
         raise ValueError("q_out must match q")
     max_position = cos_sin_cache.numel() // D
     num_slots = k_cache.size(0) * k_cache.size(1)
-    rc = _native.load_library().b200_qk_norm_rope_append(
+    lib = _native.load_library()
+    common = (
         q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), v.data_ptr(),
         v.stride(0), q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_weight.data_ptr(),
         k_weight.data_ptr(), float(eps), positions.data_ptr(), cos_sin_cache.data_ptr(),
         max_position, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(1),
-        slot_mapping.data_ptr(), T, Hq, Hkv, D, _DTYPES[q.dtype], num_slots, _ptr(status),
-        _stream_handle(q.device),
+        slot_mapping.data_ptr(), T, Hq, Hkv, D, _DTYPES[q.dtype],
     )
+    if fp8:  # an FP8 pool: quantise k and v with the scales register_kv_scales attached
+        k_scale, v_scale = kv_scales(k_cache)
+        rc = lib.b200_qk_norm_rope_append_fp8(*common, _ptr(k_scale), _ptr(v_scale), num_slots,
+                                              _ptr(status), _stream_handle(q.device))
+        _native.check(rc, "b200_qk_norm_rope_append_fp8")
+        return q_out
+    rc = lib.b200_qk_norm_rope_append(*common, num_slots, _ptr(status), _stream_handle(q.device))
     _native.check(rc, "b200_qk_norm_rope_append")
     return q_out
 

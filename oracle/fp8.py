@@ -12,8 +12,9 @@ element and per-tensor dequantisation scales: real = stored x scale.
 * ``f32_to_e4m3_bits`` — round to nearest even, saturate to +-448, NaN stays
   NaN (the semantics of ``cvt.rn.satfinite.e4m3x2.f32``); pinned in the tests
   against torch's own float8_e4m3fn conversion.
-* ``kv_append_fp8``    — the FP8 append: stored = e4m3(x / scale) with the
-  IEEE fp32 quotient; slots of -1 skipped (as ``kv_append``).
+* ``kv_append_fp8``    — the FP8 append: stored = e4m3(x * (1 / scale)), the
+  reciprocal rounded once to fp32, then an fp32 product; slots of -1 skipped
+  (as ``kv_append``).
 * ``dequantize``       — stored bytes -> fp32 real values.
 """
 
@@ -63,8 +64,10 @@ def kv_append_fp8(key, value, k_cache, v_cache, slot_mapping, k_scale=1.0, v_sca
     quantised; ``key``/``value`` are 16-bit storage arrays of ``dtype``."""
     kf = to_f32(key, dtype).reshape(len(key), -1)
     vf = to_f32(value, dtype).reshape(len(value), -1)
-    kq = f32_to_e4m3_bits(kf / np.float32(k_scale))
-    vq = f32_to_e4m3_bits(vf / np.float32(v_scale))
+    k_inv = np.float32(1.0) / np.float32(k_scale)  # IEEE: correctly rounded
+    v_inv = np.float32(1.0) / np.float32(v_scale)
+    kq = f32_to_e4m3_bits(kf * k_inv)
+    vq = f32_to_e4m3_bits(vf * v_inv)
     kc = k_cache.reshape(-1, kq.shape[1])
     vc = v_cache.reshape(-1, vq.shape[1])
     for i, s in enumerate(np.asarray(slot_mapping).tolist()):

@@ -38,7 +38,7 @@ def test_encode_matches_torch_round_to_nearest_even():
     assert (nan[0] & 0x7F) == 0x7F
 
 
-def test_append_semantics_skip_and_divide():
+def test_append_semantics_skip_and_scale():
     key = oracle.f32_to_bf16_bits(np.asarray([[1.0, -2.0] * 8, [3.0] * 16], np.float32))
     kc = np.zeros((4, 16), np.uint8)
     vc = np.zeros((4, 16), np.uint8)

@@ -101,3 +101,42 @@ def test_position_beyond_table_is_reported(cuda_device):
     slots = torch.arange(x["T"], dtype=torch.int32)
     _, _, _, _, status = _run(x, cuda_device, slots)
     assert int(status.item()) & _native.STATUS_POSITION_OUT_OF_RANGE
+
+
+def test_fused_step_into_fp8_pool(cuda_device):
+    """With an FP8 pool the fused kernel stores exactly what the FP8 append
+    stores for the 16-bit rows the bf16 pool receives: k after its rounding
+    to bf16, and v, each divided by its scale and rounded to E4M3."""
+    g = torch.Generator().manual_seed(23)
+    T, Hq, Hkv, D = 300, 32, 8, 128
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16).to(cuda_device)
+    q = qkv[:, : Hq * D].view(T, Hq, D)
+    k = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    pos = torch.randint(0, 8192, (T,), generator=g).to(cuda_device)
+    qw = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16).to(cuda_device)
+    kw = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16).to(cuda_device)
+    table = torch.from_numpy(oracle.cos_sin_cache(D, 8192, 1e6)).to(cuda_device)
+    slots = torch.randperm(64 * 16, generator=g)[:T].to(torch.int32)
+    slots[7] = -1
+    slots = slots.to(cuda_device)
+    kc16 = torch.zeros(64, 16, Hkv, D, dtype=torch.bfloat16, device=cuda_device)
+    vc16 = torch.zeros_like(kc16)
+    q16 = ops.qk_norm_rope_append(q, k, v, pos, qw, kw, table, 1e-6, kc16, vc16, slots)
+    kc8 = torch.zeros(64, 16, Hkv, D, dtype=torch.float8_e4m3fn, device=cuda_device)
+    vc8 = torch.zeros_like(kc8)
+    ks, vs = 0.05, 0.03
+    ops.register_kv_scales(kc8, vc8, torch.tensor([ks], device=cuda_device),
+                           torch.tensor([vs], device=cuda_device))
+    q8 = ops.qk_norm_rope_append(q, k, v, pos, qw, kw, table, 1e-6, kc8, vc8, slots)
+    torch.cuda.synchronize()
+    assert torch.equal(q8.view(torch.int16), q16.view(torch.int16))
+    s = slots.cpu().numpy()
+    valid = s >= 0
+    rows_k = storage(kc16).reshape(-1, Hkv, D)[s[valid]]
+    rows_v = storage(vc16).reshape(-1, Hkv, D)[s[valid]]
+    k_ref = np.zeros((64 * 16, Hkv * D), np.uint8)
+    v_ref = np.zeros_like(k_ref)
+    oracle.fp8.kv_append_fp8(rows_k, rows_v, k_ref, v_ref, s[valid], ks, vs)
+    assert np.array_equal(kc8.view(torch.uint8).cpu().numpy().reshape(-1, Hkv * D), k_ref)
+    assert np.array_equal(vc8.view(torch.uint8).cpu().numpy().reshape(-1, Hkv * D), v_ref)
