@@ -577,16 +577,16 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 #pragma unroll
       for (int k = 0; k < 8; ++k) mk[k] = kNegInf;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float sv[32];
-        tmem_ld32(tS + c * 32, sv);
+      for (int c = 0; c < 2; ++c) {
+        float sv[64];
+        tmem_ld64(tS + c * 64, sv);
         if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            mk[i & 7] = fmaxf(mk[i & 7], c * 32 + i < lim ? sv[i] : kNegInf);
+          for (int i = 0; i < 64; ++i)
+            mk[i & 7] = fmaxf(mk[i & 7], c * 64 + i < lim ? sv[i] : kNegInf);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mk[i & 7] = fmaxf(mk[i & 7], sv[i]);
+          for (int i = 0; i < 64; ++i) mk[i & 7] = fmaxf(mk[i & 7], sv[i]);
         }
       }
       // the softmax scale is positive, so it commutes with the maximum
