@@ -601,7 +601,9 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         rescale = true;
       }
       const float neg_base = m_used == kNegInf ? 0.f : -m_used;
-      float sk[4] = {0.f, 0.f, 0.f, 0.f};
+      // exponent arguments and row sums two columns at a time (f32x2)
+      const uint64_t scale2 = f2(scale, scale), base2 = f2(neg_base, neg_base);
+      uint64_t sk2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float sv[32];
@@ -609,20 +611,25 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float p0 = ex2_approx(fmaf(sv[2 * i], scale, neg_base));
-          float p1 = ex2_approx(fmaf(sv[2 * i + 1], scale, neg_base));
+          float x0, x1;
+          f2_split(f2_fma(f2(sv[2 * i], sv[2 * i + 1]), scale2, base2), x0, x1);
+          float p0 = ex2_approx(x0);
+          float p1 = ex2_approx(x1);
           if (need_mask) {
             p0 = c * 32 + 2 * i < lim ? p0 : 0.f;
             p1 = c * 32 + 2 * i + 1 < lim ? p1 : 0.f;
           }
-          sk[i & 3] += p0 + p1;
+          sk2[i & 1] = f2_add(sk2[i & 1], f2(p0, p1));
           pk[i] = pack2<M>(p0, p1);
         }
         // P over S: chunk c's 32 values -> 16 columns at 16c, which only
         // overlap S columns this row has already read
         tmem_st16(tS + c * 16, pk);
       }
-      const float sum = (sk[0] + sk[1]) + (sk[2] + sk[3]);
+      float s0, s1, s2, s3;
+      f2_split(sk2[0], s0, s1);
+      f2_split(sk2[1], s2, s3);
+      const float sum = (s0 + s1) + (s2 + s3);
       l = l * alpha + sum;
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
