@@ -786,12 +786,19 @@ def run_config4(args, rank, world, local_rank):
         raise SystemExit("--gpus must divide 8 KV heads")
     free, _ = torch.cuda.mem_get_info(device)
     layers = 64
+    fp8 = args.kv_dtype == "fp8"
     w = workloads.config4_layers(device, tp=world, layers=layers,
-                                 memory_budget=max(0, free - (12 << 30)))
+                                 memory_budget=max(0, free - (12 << 30)),
+                                 kv_dtype=torch.float8_e4m3fn if fp8 else None)
     Hq, Hkv = 64 // world, 8 // world
-    backend = B200PagedBackend(Hq, Hkv, HEAD_DIM, BLOCK_SIZE, torch.bfloat16)
+    backend = B200PagedBackend(Hq, Hkv, HEAD_DIM, BLOCK_SIZE, torch.bfloat16,
+                               kv_cache_dtype=torch.float8_e4m3fn if fp8 else None)
     plan = backend.build_plan(w.common_metadata())
     caches = [w.layer(l) for l in range(layers)]
+    if fp8:
+        one = torch.ones(1, device=device)
+        for kc, vc in caches:
+            ops.register_kv_scales(kc, vc, one, one)
     stream = torch.cuda.current_stream(device)
 
     def step():
@@ -847,10 +854,12 @@ def run_config4(args, rank, world, local_rank):
         "metric": METRIC + " (config 4, 64 layers)", "value": round(total / (ms * 1e-3) / 1e9, 1),
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "bf16 (KV cache fp8-e4m3)" if fp8 else "bf16",
+        "data": "synthetic",
         "tokens_per_s": round(512 / (ms * 1e-3), 1),
         "config": {"workload": "config4: Qwen3-32B heads (64 q / 8 KV, D 128), 64 layers of KV "
-                               "append + paged decode per step, B 512, ctx U[1024, 8192], bs 16",
+                               "append + paged decode per step, B 512, ctx U[1024, 8192], bs 16"
+                               + ("; KV pool FP8 E4M3" if fp8 else ""),
                    "parallelism": f"tp{world}: KV heads sharded, {Hq} q / {Hkv} KV heads per "
                                   "rank, no data-path collective",
                    "pool_blocks_per_layer": w.pool_blocks,

@@ -303,20 +303,23 @@ class LayeredDecode:
 
 
 def config4_layers(device, *, tp=8, batch=512, layers=64, seed=SEED_BASE + 4,
-                   memory_budget=None, dtype=torch.bfloat16) -> LayeredDecode:
+                   memory_budget=None, dtype=torch.bfloat16,
+                   kv_dtype=None) -> LayeredDecode:
     """Qwen3-32B tensor-parallel decode, all layers of one rank: Hq 64/tp,
     Hkv 8/tp, B 512, context U[1024, 8192], bs 16. The per-layer pool holds
     every block the batch needs when ``memory_budget`` bytes allow (tp >= 4
     on a 180 GB B200); otherwise it is as large as the budget allows and the
     block tables are sampled with replacement (HBM traffic is unchanged: the
-    footprint is far beyond L2)."""
+    footprint is far beyond L2). ``kv_dtype=torch.float8_e4m3fn`` gives an
+    FP8 pool (N(0,1) values rounded to E4M3, scale 1)."""
     device = torch.device(device)
     Hq, Hkv, D, bs = 64 // tp, 8 // tp, 128, 16
     g = _generator(seed, torch.device("cpu"))
     ctx = torch.randint(1024, 8193, (batch,), generator=g).tolist()
     counts = [(c + bs - 1) // bs for c in ctx]
     need = sum(counts)
-    block_bytes = bs * Hkv * D * torch.tensor([], dtype=dtype).element_size()
+    kv_dtype = dtype if kv_dtype is None else kv_dtype  # torch.float8_e4m3fn: FP8 pool
+    block_bytes = bs * Hkv * D * torch.tensor([], dtype=kv_dtype).element_size()
     if memory_budget is None:
         memory_budget = need * block_bytes * 2 * layers
     pool = max(1, min(need, int(memory_budget // (block_bytes * 2 * layers))))
@@ -331,11 +334,11 @@ def config4_layers(device, *, tp=8, batch=512, layers=64, seed=SEED_BASE + 4,
         cursor += n
         table[i, :n] = torch.tensor(row, dtype=torch.int32)
         slots.append(row[(ctx[i] - 1) // bs] * bs + (ctx[i] - 1) % bs)
-    kv = torch.empty((2, layers, pool, bs, Hkv, D), dtype=dtype, device=device)
+    kv = torch.empty((2, layers, pool, bs, Hkv, D), dtype=kv_dtype, device=device)
     gen = _generator(seed, device)
     for i in range(2):
         for l in range(layers):
-            kv[i, l].copy_(_randn(kv[i, l].shape, gen, device, dtype))
+            kv[i, l].copy_(_randn(kv[i, l].shape, gen, device, dtype).to(kv_dtype))
     return LayeredDecode(
         kv_cache=kv, q=_randn((batch, Hq, D), gen, device, dtype),
         key=_randn((batch, Hkv, D), gen, device, dtype),

@@ -129,6 +129,25 @@ def test_fp8_cache_arguments_checked_before_launch():
                                       None) == _native.B200_OK
 
 
+def test_fused_fp8_step_rejects_bad_arguments():
+    lib = _native.load_library()
+    args = [0x1000, 6144, 128, 0x2000, 6144, 0x3000, 6144, 0x4000, 4096, 128, 0x5000, 0x6000,
+            1e-6, 0x7000, 0x8000, 4096, 0x9000, 0xA000, 1024, 0xB000, 4, 32, 8, 128,
+            _native.DTYPE_BFLOAT16, None, None, 64, None, None]
+    bad = list(args)
+    bad[23] = 64  # head_dim
+    assert lib.b200_qk_norm_rope_append_fp8(*bad) == _native.B200_ERR_UNSUPPORTED
+    bad = list(args)
+    bad[18] = 1028  # cache slot stride not a multiple of 8 elements
+    assert lib.b200_qk_norm_rope_append_fp8(*bad) == _native.B200_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[16] = 0x9008  # k_cache not 16-byte aligned
+    assert lib.b200_qk_norm_rope_append_fp8(*bad) == _native.B200_ERR_INVALID_ARGUMENT
+    bad = list(args)
+    bad[20] = 0  # no tokens: a successful no-op
+    assert lib.b200_qk_norm_rope_append_fp8(*bad) == _native.B200_OK
+
+
 def test_status_description():
     assert _native.describe_status(0) == "ok"
     text = _native.describe_status(_native.STATUS_WAIT_TIMEOUT | _native.STATUS_PAGE_OUT_OF_RANGE)
