@@ -8,18 +8,21 @@
 //
 // Design (HBM-bound: ~4 FLOP per byte of KV):
 //   * One CTA per (sequence, KV head, KV partition). The group of q heads
-//     that share the KV head are the rows of a 16-row MMA tile, so each K/V
-//     byte is read from HBM exactly once per step.
+//     that share the KV head are the columns (N = 8 per MMA) of every MMA,
+//     so each K/V byte is read from HBM exactly once per step.
 //   * 4 warps per CTA, each an independent flash-decoding worker over an
 //     interleaved subset of the partition's 16-token tiles. Lane 0 of each
 //     warp streams its tiles into a 3-stage ring of shared-memory buffers
 //     with 4 TMA box loads per tile (K/V x two 64-element halves of
 //     head_dim, 128-byte swizzle), completing on one mbarrier per stage.
-//   * QK^T and PV run on mma.sync m16n8k16 with fp32 accumulation; K comes
-//     through ldmatrix, V through ldmatrix.trans; P stays in registers
-//     (accumulator layout of QK^T == A-operand layout of PV).
-//   * Online softmax in the exp2 domain with quad-lane shuffles; warps are
-//     merged through shared memory at the end. With more than one
+//   * The KV tile is the A operand (M = 16 tokens or 16 d rows): S^T = K Q^T
+//     with K through ldmatrix and Q^T (N = 8 heads) in registers, then
+//     O^T += V^T P^T with V through ldmatrix.trans. P^T comes out of the QK
+//     accumulator as (token, head) and two movmatrix.trans per tile turn it
+//     into the B operand. A GQA group of 4 fills half of each MMA's N.
+//   * Online softmax in the exp2 domain per head column: the tile maximum is
+//     an in-thread max over 2 tokens plus 3 shuffles over the 8 lanes holding
+//     the other tokens; warps are merged through shared memory at the end. With more than one
 //     partition the CTA writes an fp32 partial output plus log2-sum-exp and
 //     decode_reduce_kernel merges partitions.
 //   * Every mbarrier wait is bounded (kWaitTimeoutNs); a timeout sets
@@ -37,6 +40,14 @@ namespace b200 {
 
 __device__ __forceinline__ uint32_t ld_u32(const void* p) {
   return __ldg(reinterpret_cast<const uint32_t*>(p));
+}
+
+// Transpose of an 8x8 16-bit matrix held one packed pair per lane in the MMA
+// accumulator layout (lane (g, q): row g, columns 2q, 2q+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 // Zeroes the 16-bit halves of a packed pair whose token index (tok for the
@@ -66,14 +77,14 @@ __device__ __forceinline__ uint32_t to_f16_or_same(uint32_t w, T tag) {
 // as fp16, and the dequantisation scales fold into the softmax scale (K)
 // and the final normalisation (V). Fragment layouts for FP8:
 //   K: ldmatrix (no transpose) over 16-byte rows gives lane (g, q) the 4
-//      bytes d = 16c + 4q .. 4q+3 of token g; they serve as the B fragment's
-//      k indices {2q, 2q+1} and {8+2q, 9+2q}, so the q fragment is loaded
+//      bytes d = 16c + 4q .. 4q+3 of token g; they serve as the A fragment's
+//      k indices {2q, 2q+1} and {8+2q, 9+2q}, so the Q^T fragment is loaded
 //      with the same permutation of d within each 16-element chunk c.
 //   V: ldmatrix.trans at 16-bit granularity gives lane (g, q) the byte pairs
 //      (d = 16c + 2g, 16c + 2g + 1) of tokens 2q and 2q+1; one byte permute
-//      regroups them by d, giving B fragments for column d = 16c + 2g (even
-//      MMA) and 16c + 2g + 1 (odd MMA). The accumulator of chunk c's even
-//      and odd MMAs together holds d = 16c + 4q .. 16c + 4q + 3.
+//      regroups them by d, giving A fragments whose row g is d = 16c + 2g
+//      (even m-tile) or 16c + 2g + 1 (odd m-tile); rows g + 8 come from
+//      chunk c + 1. The merge writes each accumulator to its d.
 template <typename T, bool kHiRows, bool kFp8>
 __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -131,30 +142,25 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
   }
   __syncthreads();
 
-  // ---- Q fragments (A operand, rows = q heads of this KV head's group) ----
-  const int gr = lane >> 2;  // row within the MMA tile
-  const int tq = lane & 3;   // column pair index
+  // ---- Q^T fragments (B operand: k = head_dim, n = 8 q heads of the group) ----
+  constexpr int NT = kHiRows ? 2 : 1;  // 8-head n-tiles
+  const int gr = lane >> 2;  // fragment row (token or d) / column (head) index
+  const int tq = lane & 3;   // column-pair index
   const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_seq_stride +
                 (int64_t)(kvh * p.group) * p.q_head_stride;
-  uint32_t qa[8][4];
+  uint32_t qf[NT][8][2];
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    // 16-bit caches: k pairs (2q, 2q+1) and (8+2q, 9+2q) of chunk kk are
-    // d = 16kk + 2q (+1) and 16kk + 8 + 2q (+1). FP8: d = 16kk + 4q .. 4q+3.
-    const int d0 = kFp8 ? kk * 16 + tq * 4 : kk * 16 + tq * 2;
-    const int d1 = kFp8 ? d0 + 2 : d0 + 8;
-    const bool lo_ok = gr < p.group;
-    qa[kk][0] = lo_ok ? to_f16_or_same<kFp8>(ld_u32(qb + gr * p.q_head_stride + d0), T()) : 0u;
-    qa[kk][2] = lo_ok ? to_f16_or_same<kFp8>(ld_u32(qb + gr * p.q_head_stride + d1), T()) : 0u;
-    if (kHiRows) {
-      const bool hi_ok = gr + 8 < p.group;
-      qa[kk][1] =
-          hi_ok ? to_f16_or_same<kFp8>(ld_u32(qb + (gr + 8) * p.q_head_stride + d0), T()) : 0u;
-      qa[kk][3] =
-          hi_ok ? to_f16_or_same<kFp8>(ld_u32(qb + (gr + 8) * p.q_head_stride + d1), T()) : 0u;
-    } else {
-      qa[kk][1] = 0u;
-      qa[kk][3] = 0u;
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = nt * 8 + gr;
+    const bool ok_h = h < p.group;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      // 16-bit caches: k pairs (2q, 2q+1) and (8+2q, 9+2q) of chunk kk are
+      // d = 16kk + 2q (+1) and 16kk + 8 + 2q (+1). FP8: d = 16kk + 4q .. 4q+3.
+      const int d0 = kFp8 ? kk * 16 + tq * 4 : kk * 16 + tq * 2;
+      const int d1 = kFp8 ? d0 + 2 : d0 + 8;
+      qf[nt][kk][0] = ok_h ? to_f16_or_same<kFp8>(ld_u32(qb + h * p.q_head_stride + d0), T()) : 0u;
+      qf[nt][kk][1] = ok_h ? to_f16_or_same<kFp8>(ld_u32(qb + h * p.q_head_stride + d1), T()) : 0u;
     }
   }
   float scale_log2 = p.scale_log2;
@@ -200,10 +206,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
   int issued = prologue;
 
   const float kNegInf = -INFINITY;
-  float m_lo = kNegInf, m_hi = kNegInf, l_lo = 0.f, l_hi = 0.f;
-  float o[16][4];
+  // softmax state per head column of this thread: heads nt*8 + 2q + c
+  float m_run[NT][2], l_run[NT][2];
+  // O^T accumulators: per n-tile, 8 m-tiles of 16 d rows x 8 heads
+  float o[NT][8][4];
 #pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = kNegInf;
+    l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+  }
 
   int consumed = 0;
   bool ok = true;
@@ -221,149 +234,139 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
     const int t = warp + j * kDecodeWarps;
     const int valid = min(kTileTokens, tok_end - (tok_begin + t * kTileTokens));
 
-    // ---- S = Q K^T (16 rows x 16 tokens) ----
-    float s0[4] = {0.f, 0.f, 0.f, 0.f};
-    float s1[4] = {0.f, 0.f, 0.f, 0.f};
+    // ---- S^T = K Q^T (16 tokens x 8 heads per n-tile); A = K from the tile ----
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
     {
-      const int r = (lane & 7) + ((lane >> 4) << 3);
-      const int csel = (lane >> 3) & 1;
+      // matrices of one x4 load: (tokens 0-7 | 8-15) x (k columns 0-7 | 8-15)
+      const int r = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int csel = lane >> 4;
       if constexpr (kFp8) {
-        // matrices: (tokens 0-7 | 8-15) x (chunk cc | cc+1) of 16 d each
+        // one 16-byte row chunk holds 16 d of one token: chunks cc and cc+1
 #pragma unroll
         for (int cc = 0; cc < 8; cc += 2) {
-          uint32_t r0, r1, r2, r3, b0, b1;
+          uint32_t r0, r1, r2, r3;
           ldmatrix_x4(kb + swz128(r, cc + csel), r0, r1, r2, r3);
-          e4m3x4_to_f16(r0, b0, b1);
-          Elem<M>::mma(s0, qa[cc], b0, b1);
-          e4m3x4_to_f16(r1, b0, b1);
-          Elem<M>::mma(s0, qa[cc + 1], b0, b1);
-          e4m3x4_to_f16(r2, b0, b1);
-          Elem<M>::mma(s1, qa[cc], b0, b1);
-          e4m3x4_to_f16(r3, b0, b1);
-          Elem<M>::mma(s1, qa[cc + 1], b0, b1);
+          uint32_t a[4];
+          e4m3x4_to_f16(r0, a[0], a[2]);  // tokens g: d 16cc + 4q .. 4q+3
+          e4m3x4_to_f16(r1, a[1], a[3]);  // tokens g + 8
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Elem<M>::mma(sc[nt], a, qf[nt][cc][0], qf[nt][cc][1]);
+          e4m3x4_to_f16(r2, a[0], a[2]);
+          e4m3x4_to_f16(r3, a[1], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            Elem<M>::mma(sc[nt], a, qf[nt][cc + 1][0], qf[nt][cc + 1][1]);
         }
       } else {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t addr = kb + (kk >> 2) * kHalfTileBytes +
                                 swz128(r, ((kk & 3) << 1) + csel);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(addr, b0, b1, b2, b3);
-          Elem<M>::mma(s0, qa[kk], b0, b1);
-          Elem<M>::mma(s1, qa[kk], b2, b3);
+          uint32_t a[4];
+          ldmatrix_x4(addr, a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Elem<M>::mma(sc[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
         }
       }
     }
+
+    // ---- online softmax per head column (max over the 16 tokens of the tile) ----
+    uint32_t pb[NT][2];  // P^T as the B operand of PV (after the transpose)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      s0[i] *= scale_log2;
-      s1[i] *= scale_log2;
-    }
-    if (valid < kTileTokens) {
-      const int c0 = tq * 2;
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (c0 + (i & 1) >= valid) s0[i] = kNegInf;
-        if (8 + c0 + (i & 1) >= valid) s1[i] = kNegInf;
+      for (int i = 0; i < 4; ++i) sc[nt][i] *= scale_log2;
+      if (valid < kTileTokens) {
+        if (gr >= valid) sc[nt][0] = sc[nt][1] = kNegInf;
+        if (gr + 8 >= valid) sc[nt][2] = sc[nt][3] = kNegInf;
       }
+      float pr[2][2];  // [token g | g+8][head column c]
+      bool moved = false;
+      float alpha[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float mx = fmaxf(sc[nt][c], sc[nt][2 + c]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[nt][c], mx);
+        const float base = m_new == kNegInf ? 0.f : m_new;
+        alpha[c] = fast_exp2(m_run[nt][c] - base);
+        pr[0][c] = fast_exp2(sc[nt][c] - base);
+        pr[1][c] = fast_exp2(sc[nt][2 + c] - base);
+        l_run[nt][c] = l_run[nt][c] * alpha[c] + (pr[0][c] + pr[1][c]);
+        moved |= m_new != m_run[nt][c];
+        m_run[nt][c] = m_new;
+      }
+      // alpha is exactly 1 unless a running max moved: skip the multiplies
+      // on the (usual) tiles where none did
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[nt][mt][0] *= alpha[0];
+          o[nt][mt][1] *= alpha[1];
+          o[nt][mt][2] *= alpha[0];
+          o[nt][mt][3] *= alpha[1];
+        }
+      }
+      // P^T rows (tokens) x columns (heads) in accumulator layout -> transpose
+      // to the B layout (k = tokens 2q, 2q+1 | 8+2q, 9+2q; n = head g)
+      pb[nt][0] = movmatrix_trans(Elem<M>::pack(pr[0][0], pr[0][1]));
+      pb[nt][1] = movmatrix_trans(Elem<M>::pack(pr[1][0], pr[1][1]));
     }
 
-    // ---- online softmax (rows gr and gr + 8) ----
-    uint32_t pa[4];
+    // ---- O^T += V^T P^T (16 d rows x 8 heads per m-tile); A = V^T ----
     {
-      float mx = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_lo, mx);
-      const float base = m_new == kNegInf ? 0.f : m_new;
-      const float alpha = fast_exp2(m_lo - base);
-      const float p0 = fast_exp2(s0[0] - base), p1 = fast_exp2(s0[1] - base);
-      const float p2 = fast_exp2(s1[0] - base), p3 = fast_exp2(s1[1] - base);
-      l_lo = l_lo * alpha + (p0 + p1) + (p2 + p3);
-      // alpha is exactly 1 unless the running max moved: skip the 32
-      // multiplies on the (usual) tiles where no row's max moved
-      if (__any_sync(0xffffffffu, m_new != m_lo)) {
+      // matrices of one x4.trans load: (tokens 0-7 | 8-15) x (two 8-column
+      // chunks); lane (g, q) receives tokens 2q, 2q+1 of column g
+      const int r = (lane & 7) + ((lane >> 4) << 3);
+      const int csel = (lane >> 3) & 1;
+      if constexpr (kFp8) {
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          o[n][0] *= alpha;
-          o[n][1] *= alpha;
-        }
-      }
-      m_lo = m_new;
-      pa[0] = Elem<M>::pack(p0, p1);
-      pa[2] = Elem<M>::pack(p2, p3);
-    }
-    if (kHiRows) {
-      float mx = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_hi, mx);
-      const float base = m_new == kNegInf ? 0.f : m_new;
-      const float alpha = fast_exp2(m_hi - base);
-      const float p0 = fast_exp2(s0[2] - base), p1 = fast_exp2(s0[3] - base);
-      const float p2 = fast_exp2(s1[2] - base), p3 = fast_exp2(s1[3] - base);
-      l_hi = l_hi * alpha + (p0 + p1) + (p2 + p3);
-      if (__any_sync(0xffffffffu, m_new != m_hi)) {
+        for (int pp = 0; pp < 4; ++pp) {
+          // chunks 2pp, 2pp+1 (d 32pp .. 32pp + 31): even / odd d m-tiles
+          uint32_t v[4];
+          ldmatrix_x4_trans(vb + swz128(r, 2 * pp + csel), v[0], v[1], v[2], v[3]);
+          uint32_t ae[4], ao[4];
+          e4m3x4_to_f16(__byte_perm(v[0], 0, 0x3120), ae[0], ao[0]);  // d 32pp + 2g, tok 2q..
+          e4m3x4_to_f16(__byte_perm(v[1], 0, 0x3120), ae[1], ao[1]);  // d 32pp + 16 + 2g
+          e4m3x4_to_f16(__byte_perm(v[2], 0, 0x3120), ae[2], ao[2]);  // tokens 8 + 2q..
+          e4m3x4_to_f16(__byte_perm(v[3], 0, 0x3120), ae[3], ao[3]);
+          if (valid < kTileTokens) {  // never-written slots may hold NaN bytes
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          o[n][2] *= alpha;
-          o[n][3] *= alpha;
-        }
-      }
-      m_hi = m_new;
-      pa[1] = Elem<M>::pack(p0, p1);
-      pa[3] = Elem<M>::pack(p2, p3);
-    } else {
-      pa[1] = 0u;
-      pa[3] = 0u;
-    }
-
-    // ---- O += P V (16 rows x 128 dims) ----
-    if constexpr (kFp8) {
-      const int r = (lane & 7) + (((lane >> 3) & 1) << 3);
-      const int csel = lane >> 4;
-#pragma unroll
-      for (int cc = 0; cc < 8; cc += 2) {
-        // v0 / v1: tokens 0-7 / 8-15 of chunk cc; v2 / v3: the same of cc+1
-        uint32_t v[4];
-        ldmatrix_x4_trans(vb + swz128(r, cc + csel), v[0], v[1], v[2], v[3]);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t e0, o0, e1, o1;  // even / odd d column, tokens 2q.. / 8+2q..
-          e4m3x4_to_f16(__byte_perm(v[2 * h], 0, 0x3120), e0, o0);
-          e4m3x4_to_f16(__byte_perm(v[2 * h + 1], 0, 0x3120), e1, o1);
-          if (valid < kTileTokens) {
-            // never-written slots past the sequence end may hold NaN bytes
-            e0 = mask_pair(e0, tq * 2, valid);
-            o0 = mask_pair(o0, tq * 2, valid);
-            e1 = mask_pair(e1, 8 + tq * 2, valid);
-            o1 = mask_pair(o1, 8 + tq * 2, valid);
+            for (int i = 0; i < 4; ++i) {
+              const int tok = (i >> 1) * 8 + tq * 2;
+              ae[i] = mask_pair(ae[i], tok, valid);
+              ao[i] = mask_pair(ao[i], tok, valid);
+            }
           }
-          Elem<M>::mma(o[2 * (cc + h)], pa, e0, e1);
-          Elem<M>::mma(o[2 * (cc + h) + 1], pa, o0, o1);
-        }
-      }
-    } else {
-      const int r = (lane & 7) + (((lane >> 3) & 1) << 3);
-      const int csel = lane >> 4;
 #pragma unroll
-      for (int dn = 0; dn < 8; ++dn) {
-        const int c = dn * 2 + csel;
-        const uint32_t addr = vb + (c >> 3) * kHalfTileBytes + swz128(r, c & 7);
-        uint32_t v0, v1, v2, v3;
-        ldmatrix_x4_trans(addr, v0, v1, v2, v3);
-        if (valid < kTileTokens) {
-          // Rows past the sequence end may hold never-written cache memory
-          // (possibly NaN bit patterns) and P = 0 does not cancel NaN, so
-          // clear those V elements in registers: v0/v2 hold tokens 2tq and
-          // 2tq+1 (low/high half), v1/v3 tokens 8+2tq and 9+2tq.
-          v0 = mask_pair(v0, tq * 2, valid);
-          v2 = mask_pair(v2, tq * 2, valid);
-          v1 = mask_pair(v1, 8 + tq * 2, valid);
-          v3 = mask_pair(v3, 8 + tq * 2, valid);
+          for (int nt = 0; nt < NT; ++nt) {
+            Elem<M>::mma(o[nt][2 * pp], ae, pb[nt][0], pb[nt][1]);
+            Elem<M>::mma(o[nt][2 * pp + 1], ao, pb[nt][0], pb[nt][1]);
+          }
         }
-        Elem<M>::mma(o[2 * dn], pa, v0, v1);
-        Elem<M>::mma(o[2 * dn + 1], pa, v2, v3);
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int c = mt * 2 + csel;  // 8-element column chunk (d 8c .. 8c + 7)
+          const uint32_t addr = vb + (c >> 3) * kHalfTileBytes + swz128(r, c & 7);
+          uint32_t a[4];
+          ldmatrix_x4_trans(addr, a[0], a[1], a[2], a[3]);
+          if (valid < kTileTokens) {
+            // Rows past the sequence end may hold never-written cache memory
+            // (possibly NaN bit patterns) and P = 0 does not cancel NaN, so
+            // clear those V elements in registers.
+            a[0] = mask_pair(a[0], tq * 2, valid);
+            a[1] = mask_pair(a[1], tq * 2, valid);
+            a[2] = mask_pair(a[2], 8 + tq * 2, valid);
+            a[3] = mask_pair(a[3], 8 + tq * 2, valid);
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Elem<M>::mma(o[nt][mt], a, pb[nt][0], pb[nt][1]);
+        }
       }
     }
 
@@ -385,47 +388,41 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
   }
 
   // ---- merge the warps' partial softmax states ----
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  // each lane summed only its two tokens per tile: add over the 8 lanes g
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      l_run[nt][c] += __shfl_xor_sync(0xffffffffu, l_run[nt][c], 4);
+      l_run[nt][c] += __shfl_xor_sync(0xffffffffu, l_run[nt][c], 8);
+      l_run[nt][c] += __shfl_xor_sync(0xffffffffu, l_run[nt][c], 16);
+    }
   __syncthreads();  // every warp is done with the stage buffers
 
   float* ml = reinterpret_cast<float*>(smem);                   // [W][2][16]
   float* mo = reinterpret_cast<float*>(smem) + kDecodeWarps * 32;  // [W][16][kMergeStride]
-  if (tq == 0) {
-    if (gr < p.group) {
-      ml[warp * 32 + gr] = m_lo;
-      ml[warp * 32 + 16 + gr] = l_lo;
-    }
-    if (kHiRows && gr + 8 < p.group) {
-      ml[warp * 32 + gr + 8] = m_hi;
-      ml[warp * 32 + 16 + gr + 8] = l_hi;
-    }
-  }
-  if constexpr (kFp8) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int d = c * 16 + tq * 4;
-      if (gr < p.group)
-        *reinterpret_cast<float4*>(&mo[(warp * 16 + gr) * kMergeStride + d]) =
-            make_float4(o[2 * c][0], o[2 * c + 1][0], o[2 * c][1], o[2 * c + 1][1]);
-      if (kHiRows && gr + 8 < p.group)
-        *reinterpret_cast<float4*>(&mo[(warp * 16 + gr + 8) * kMergeStride + d]) =
-            make_float4(o[2 * c][2], o[2 * c + 1][2], o[2 * c][3], o[2 * c + 1][3]);
-    }
-  } else {
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      const int d = n * 8 + tq * 2;
-      if (gr < p.group)
-        *reinterpret_cast<float2*>(&mo[(warp * 16 + gr) * kMergeStride + d]) =
-            make_float2(o[n][0], o[n][1]);
-      if (kHiRows && gr + 8 < p.group)
-        *reinterpret_cast<float2*>(&mo[(warp * 16 + gr + 8) * kMergeStride + d]) =
-            make_float2(o[n][2], o[n][3]);
+    for (int c = 0; c < 2; ++c) {
+      const int head = nt * 8 + tq * 2 + c;
+      if (head < p.group) {
+        if (gr == 0) {
+          ml[warp * 32 + head] = m_run[nt][c];
+          ml[warp * 32 + 16 + head] = l_run[nt][c];
+        }
+        float* row = &mo[(warp * 16 + head) * kMergeStride];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          // bf16: m-tile mt holds d = 16 mt + g (+8); FP8: m-tile 2pp + e
+          // holds d = 32 pp + 2g + e (+16)
+          const int d_lo = kFp8 ? 32 * (mt >> 1) + 2 * gr + (mt & 1) : 16 * mt + gr;
+          const int d_hi = kFp8 ? d_lo + 16 : d_lo + 8;
+          row[d_lo] = o[nt][mt][c];
+          row[d_hi] = o[nt][mt][2 + c];
+        }
+      }
     }
-  }
   __syncthreads();
 
   for (int idx = threadIdx.x; idx < p.group * kHeadDim; idx += blockDim.x) {
