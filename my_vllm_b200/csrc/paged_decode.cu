@@ -86,7 +86,7 @@ __device__ __forceinline__ uint32_t to_f16_or_same(uint32_t w, T tag) {
 //      (even m-tile) or 16c + 2g + 1 (odd m-tile); rows g + 8 come from
 //      chunk c + 1. The merge writes each accumulator to its d.
 template <typename T, bool kHiRows, bool kFp8>
-__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 3 : 2)
+__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? (kHiRows ? 3 : 4) : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v,
                         const DecodeParams p) {

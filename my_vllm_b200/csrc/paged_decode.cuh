@@ -16,11 +16,12 @@ constexpr int kDecodeStageBytes = 4 * kHalfTileBytes;  // K lo/hi + V lo/hi = 8 
 constexpr int kDecodeStageArenaBytes = kDecodeWarps * kDecodeStages * kDecodeStageBytes;
 // FP8 E4M3 caches: a 16-token tile of K (or V) is 16 rows x 128 bytes, one TMA
 // box. Per-token work is the same as for 16-bit caches but the bytes halve,
-// so the FP8 kernel runs 3 CTAs per SM (more warps to hide MMA and convert
-// latency) with 4 stages of 4 KiB per warp: 192 KiB in flight per SM, as
-// the 16-bit kernel's 2 CTAs x 4 warps x 3 x 8 KiB.
+// so the FP8 kernel runs 4 CTAs per SM (more warps to hide MMA and convert
+// latency; 3 for groups of more than 8 q heads, whose registers allow no
+// more) with 3 stages of 4 KiB per warp: 192 KiB in flight per SM, as the
+// 16-bit kernel's 2 CTAs x 4 warps x 3 x 8 KiB.
 constexpr int kFp8TileBytes = kTileTokens * 128;
-constexpr int kFp8Stages = 4;
+constexpr int kFp8Stages = 3;
 constexpr int kFp8StageBytes = 2 * kFp8TileBytes;  // K + V = 4 KiB
 constexpr int kFp8StageArenaBytes = kDecodeWarps * kFp8Stages * kFp8StageBytes;
 // Longest KV partition one CTA takes; the planner splits longer contexts.
@@ -33,7 +34,7 @@ constexpr int decode_smem_bytes(bool fp8) {
 }
 static_assert(kDecodeWarps * (32 + 16 * kMergeStride) * 4 <= kFp8StageArenaBytes,
               "merge area must fit in the stage arena");
-static_assert(3 * decode_smem_bytes(true) <= 227 * 1024, "3 FP8 CTAs per SM");
+static_assert(4 * (decode_smem_bytes(true) + 1024) <= 228 * 1024, "4 FP8 CTAs per SM");
 
 struct DecodeParams {
   const void* q;
