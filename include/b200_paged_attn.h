@@ -218,15 +218,16 @@ typedef struct b200_decode_plan {
  * is assumed to be max_kv_len long) on the current device. Host-only: the
  * engine knows both from its per-step block counts. `force_num_parts` > 0
  * pins the split count (tests); 0 lets the planner fill the SMs and cut the
- * longest sequences into pieces small enough to balance. Replaces the decode
- * half of FlashInferBackend.build_plan
- * (nanovllm/layers/attention_backend.py:827-839).
+ * longest sequences into pieces small enough to balance. `kv_fp8` = 1 plans
+ * for an FP8 E4M3 cache (its kernel holds twice as many CTAs per SM, so
+ * small batches split sooner). Replaces the decode half of
+ * FlashInferBackend.build_plan (nanovllm/layers/attention_backend.py:827-839).
  */
 B200_API int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads,
                            int32_t num_kv_heads, int32_t head_dim,
                            int32_t block_size, int32_t max_kv_len,
                            int64_t total_kv_tokens, int32_t force_num_parts,
-                           b200_decode_plan* plan);
+                           int32_t kv_fp8, b200_decode_plan* plan);
 
 /*
  * Paged decode attention: one query token per sequence.

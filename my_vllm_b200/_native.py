@@ -29,7 +29,7 @@ DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
 DTYPE_FP8_E4M3 = 2
 
-ABI_VERSION = 200
+ABI_VERSION = 201
 
 # Size of the scratch array built into the library for
 # b200_paged_decode_noalloc (B200_NOALLOC_DECODE_SCRATCH_BYTES).
@@ -116,7 +116,7 @@ _SIGNATURES = {
         _I32,
     ),
     "b200_paged_decode_plan": (
-        [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32, ctypes.POINTER(DecodePlan)],
+        [_I32, _I32, _I32, _I32, _I32, _I32, _I64, _I32, _I32, ctypes.POINTER(DecodePlan)],
         _I32,
     ),
     "b200_paged_decode": (

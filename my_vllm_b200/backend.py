@@ -294,6 +294,7 @@ class B200PagedBackend(AttentionBackend):
                 common.num_decode_seqs, self.num_q_heads, self.num_kv_heads, self.head_dim,
                 self.block_size, self._decode_max_kv_len(common), self.decode_num_parts,
                 total_kv_tokens=self._decode_total_kv_tokens(common),
+                kv_fp8=self.kv_cache_dtype == ops.FP8_DTYPE,
             )
         return B200PagedMetadata(
             common.query_start_loc, common.seq_lens, common.block_tables, decode_plan
@@ -501,7 +502,8 @@ class B200PagedBackend(AttentionBackend):
         max_kv_len = max_pages * self.block_size
         decode_plan = ops.plan_decode(batch_size, self.num_q_heads, self.num_kv_heads,
                                       self.head_dim, self.block_size, max_kv_len,
-                                      self.decode_num_parts)
+                                      self.decode_num_parts,
+                                      kv_fp8=self.kv_cache_dtype == ops.FP8_DTYPE)
         workspace = None
         if decode_plan.workspace_bytes:
             workspace = torch.empty(decode_plan.workspace_bytes, dtype=torch.uint8,

@@ -182,7 +182,7 @@ void set_last_error(const std::string& message) { g_last_error = message; }
 
 extern "C" {
 
-int b200_abi_version(void) { return 200; }
+int b200_abi_version(void) { return 201; }
 
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -377,7 +377,7 @@ int b200_store_kvcache_fp8(const void* key, int64_t key_row_stride, const void* 
 int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t head_dim, int32_t block_size, int32_t max_kv_len,
                            int64_t total_kv_tokens, int32_t force_num_parts,
-                           b200_decode_plan* plan) {
+                           int32_t kv_fp8, b200_decode_plan* plan) {
   g_last_error.clear();
   if (plan == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "plan is NULL");
   if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_kv_len <= 0)
@@ -400,14 +400,17 @@ int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv
   } else {
     // The kernel is HBM-bound: it needs bytes in flight, not full waves of
     // CTAs, and every extra partition costs a pipeline ramp plus partial
-    // outputs. So split only (a) to give every SM at least one CTA, and (b)
-    // for ragged batches, so no CTA holds more than 1/12 of the average
+    // outputs. So split only (a) to give every SM at least one CTA (two for
+    // FP8 caches, whose kernel holds 4 CTAs per SM: one KV head of 256
+    // sequences measured 0.056 ms split in two against 0.068 ms whole), and
+    // (b) for ragged batches, so no CTA holds more than 1/12 of the average
     // per-SM work (the longest sequences would otherwise finish last on a few
     // SMs; 1/12 measured best on a 124-sequence batch of U[128, 8192]).
     const int64_t units = (int64_t)num_seqs * num_kv_heads;
     const int64_t sms = sm_count();
+    const int64_t cover = kv_fp8 ? 2 * sms : sms;
     parts = min_parts;
-    if (units * parts < sms) parts = (sms + units - 1) / units;
+    if (units * parts < cover) parts = (cover + units - 1) / units;
     const int64_t max_tokens = (int64_t)num_seqs * max_kv_len;
     const int64_t total = (total_kv_tokens > 0 && total_kv_tokens < max_tokens)
                               ? total_kv_tokens : max_tokens;

@@ -367,13 +367,15 @@ def plan_decode(
     max_kv_len: int,
     force_num_parts: int = 0,
     total_kv_tokens: int = 0,
+    kv_fp8: bool = False,
 ) -> DecodePlan:
     """Choose the split-KV partition for a decode batch (host only, no sync).
-    ``total_kv_tokens`` (0 = unknown) lets the planner balance ragged batches."""
+    ``total_kv_tokens`` (0 = unknown) lets the planner balance ragged batches;
+    ``kv_fp8`` plans for an FP8 E4M3 cache."""
     plan = _native.DecodePlan()
     rc = _native.load_library().b200_paged_decode_plan(
         num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max(1, max_kv_len),
-        int(total_kv_tokens), force_num_parts, plan,
+        int(total_kv_tokens), force_num_parts, 1 if kv_fp8 else 0, plan,
     )
     _native.check(rc, "b200_paged_decode_plan")
     return DecodePlan(*plan.as_tuple())

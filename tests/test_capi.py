@@ -39,6 +39,13 @@ def test_plan_without_gpu_falls_back_to_148_sms():
     assert plan.workspace_bytes >= 32 * 32 * plan.num_parts * (128 + 1) * 4
 
 
+def test_fp8_plans_cover_two_ctas_per_sm():
+    # one KV head of 256 sequences: whole for 16-bit caches, split in two for FP8
+    assert ops.plan_decode(256, 4, 1, 128, 16, 4096).num_parts == 1
+    assert ops.plan_decode(256, 4, 1, 128, 16, 4096, kv_fp8=True).num_parts == 2
+    assert ops.plan_decode(256, 8, 2, 128, 16, 4096, kv_fp8=True).num_parts == 1
+
+
 def test_forced_split_and_limits():
     plan = ops.plan_decode(4, 8, 2, 128, 16, 1000, force_num_parts=5)
     assert plan.num_parts == 5 and plan.part_tokens * 5 >= 1000

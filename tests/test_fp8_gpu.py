@@ -64,7 +64,7 @@ def test_fp8_append_out_of_range_slot(cuda_device):
 def _fp8_decode(w, k8, v8, ks, vs, dev, parts=0):
     plan = ops.plan_decode(w.num_seqs, w.num_q_heads, w.num_kv_heads, 128, w.block_size,
                            max(w.extra["seq_lens_host"]), force_num_parts=parts,
-                           total_kv_tokens=sum(w.extra["seq_lens_host"]))
+                           total_kv_tokens=sum(w.extra["seq_lens_host"]), kv_fp8=True)
     ws = torch.empty(max(plan.workspace_bytes, 1), dtype=torch.uint8, device=dev)
     out = torch.empty_like(w.q)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
