@@ -297,3 +297,31 @@ def test_prefill_longest_first_order_covers_every_row(cuda_device, hq, hkv):
     assert int(status.item()) == 0
     expected, rows = sample_oracle(w, list(range(len(q_lens))))
     assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+@pytest.mark.parametrize("hq,hkv,bs", [(8, 8, 16), (24, 8, 16), (20, 4, 32), (32, 2, 64),
+                                        (12, 4, 16)])
+def test_decode_and_prefill_group_and_block_shapes(cuda_device, hq, hkv, bs):
+    """GQA groups 1, 3, 5, 16 and 3, block sizes 16/32/64: a decode batch (ragged,
+    with a split forced) and a prefill batch against the oracle."""
+    lens = [1, 17, 300, 1029, 4000]
+    w = workloads.small_case([1] * len(lens), lens, 0, Hq=hq, Hkv=hkv, bs=bs, device=cuda_device)
+    for parts in (0, 3):
+        plan = ops.plan_decode(len(lens), hq, hkv, 128, bs, max(lens), force_num_parts=parts,
+                               total_kv_tokens=sum(lens))
+        ws = torch.empty(max(plan.workspace_bytes, 1), dtype=torch.uint8, device=cuda_device)
+        out = torch.full_like(w.q, float("nan"))
+        ops.paged_decode(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, out, plan,
+                         128 ** -0.5, ws)
+        torch.cuda.synchronize()
+        expected, rows = sample_oracle(w, list(range(len(lens))))
+        assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    q_lens = [5, 77, 130]
+    kv = [5, 500, 1300]
+    w = workloads.small_case(q_lens, kv, len(q_lens), Hq=hq, Hkv=hkv, bs=bs, device=cuda_device)
+    out = torch.full_like(w.q, float("nan"))
+    ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, w.query_start_loc,
+                      out, max(q_lens), 128 ** -0.5)
+    torch.cuda.synchronize()
+    expected, rows = sample_oracle(w, list(range(len(q_lens))))
+    assert_close_to_oracle(out[rows], expected, w.q.dtype)
