@@ -85,8 +85,9 @@ __device__ __forceinline__ uint32_t to_f16_or_same(uint32_t w, T tag) {
 //      regroups them by d, giving A fragments whose row g is d = 16c + 2g
 //      (even m-tile) or 16c + 2g + 1 (odd m-tile); rows g + 8 come from
 //      chunk c + 1. The merge writes each accumulator to its d.
-template <typename T, bool kHiRows, bool kFp8>
-__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? (kHiRows ? 3 : 4) : 2)
+// kWideGroup: more than 8 q heads per KV head, two 8-head n-tiles per MMA step.
+template <typename T, bool kWideGroup, bool kFp8>
+__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? (kWideGroup ? 3 : 4) : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v,
                         const DecodeParams p) {
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? (kHiRows ? 3 : 4) : 
   __syncthreads();
 
   // ---- Q^T fragments (B operand: k = head_dim, n = 8 q heads of the group) ----
-  constexpr int NT = kHiRows ? 2 : 1;  // 8-head n-tiles
+  constexpr int NT = kWideGroup ? 2 : 1;  // 8-head n-tiles
   const int gr = lane >> 2;  // fragment row (token or d) / column (head) index
   const int tq = lane & 3;   // column-pair index
   const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_seq_stride +
@@ -481,11 +482,11 @@ __global__ void __launch_bounds__(kHeadDim)
   ob[d] = Elem<T>::from_float(l > 0.f ? acc / l : 0.f);
 }
 
-template <typename T, bool kHiRows, bool kFp8>
+template <typename T, bool kWideGroup, bool kFp8>
 static cudaError_t launch_typed(const CUtensorMap& mk, const CUtensorMap& mv,
                                 const DecodeParams& p, int num_kv_heads,
                                 int num_seqs, cudaStream_t stream) {
-  auto kernel = paged_decode_kernel<T, kHiRows, kFp8>;
+  auto kernel = paged_decode_kernel<T, kWideGroup, kFp8>;
   constexpr int kSmem = decode_smem_bytes(kFp8);
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kSmem);
   if (e != cudaSuccess) return e;
