@@ -12,9 +12,12 @@
 //     form two UMMA M = 128 tiles, A and B, that share every K/V tile.
 //   * warps 0-3 / 4-7: two softmax warpgroups, one per Q tile; thread t of a
 //     group owns row t = TMEM lane t, so row max and row sum need no shuffles.
-//     They stage their Q tile into shared memory (K-major, 128-byte swizzle).
+//     They stage their Q tile into shared memory (K-major, 128-byte swizzle)
+//     and hand it to the MMA warp through an mbarrier, while the producer
+//     already streams K and V.
 //   * warp 8: TMA producer streaming 128-token K and V tiles of the paged
-//     cache (8 x 16-token sub-tiles, one lane each) into separate rings: K
+//     cache (8 x 16-token sub-tiles, one lane each; page ids read from the
+//     block table four tiles at a time, a group ahead) into separate rings: K
 //     (3 stages) is released as soon as a tile's S MMAs retire and so runs two
 //     tiles ahead; V (2 stages) is released after the PV MMAs.
 //   * warp 9: allocates all 512 TMEM columns (S_A | O_A | S_B | O_B) and one
@@ -121,53 +124,86 @@ __device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int r
   return min((kv_limit + kTcKv - 1) / kTcKv, kTcCostKeys - 1);
 }
 
+// Pair costs kept in shared memory by tc_decode_unit (beyond this many pairs
+// the rank search recomputes them from the metadata).
+constexpr int kTcCachedPairs = 8192;
+constexpr int kTcScratchInts = kTcCostKeys + 4 + kTcCachedPairs;
+static_assert(kTcScratchInts * 4 <= kTcTiles * 2 * kTcHalf, "scratch lives in the Q tiles");
+
 // (sequence, row block, KV head) of grid position `pos`; `scratch` holds
-// kTcCostKeys + 2 ints of shared memory. Call with all threads of the CTA.
+// kTcScratchInts ints of 16-byte aligned shared memory. Call with all
+// threads of the CTA. One round of metadata loads, then shared memory and
+// shuffles only: the whole CTA waits on this before any load is issued.
 __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, int* scratch,
                                                int& s, int& rb, int& kvh) {
-  int* hist = scratch;  // [kTcCostKeys]
+  int* hist = scratch;                        // [kTcCostKeys]
+  int* result = scratch + kTcCostKeys;        // [2]
+  int* cost = scratch + kTcCostKeys + 4;      // [kTcCachedPairs]
   const int pairs = p.num_seqs * p.blocks_per_seq;
-  for (int i = threadIdx.x; i < kTcCostKeys; i += blockDim.x) hist[i] = 0;
+  for (int i = threadIdx.x; i < kTcCostKeys / 4; i += blockDim.x)
+    reinterpret_cast<int4*>(hist)[i] = make_int4(0, 0, 0, 0);
   __syncthreads();
-  for (int i = threadIdx.x; i < pairs; i += blockDim.x)
-    atomicAdd(&hist[tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq)], 1);
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int c = tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq);
+    if (i < kTcCachedPairs) cost[i] = c;
+    atomicAdd(&hist[c], 1);
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
+    const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x;
     const int pair_pos = pos / p.num_kv_heads;
-    // bucket of pair_pos in descending cost order: lane l owns keys [64l, 64l+64)
+    // Keys in descending order: lane l owns the chunk of keys
+    // [2048 - 64(l+1), 2048 - 64l), so lower lanes hold larger costs.
     constexpr int kPerLane = kTcCostKeys / 32;
+    const int chunk_lo = kTcCostKeys - kPerLane * (lane + 1);
     int chunk = 0;
-    for (int k = 0; k < kPerLane; ++k) chunk += hist[lane * kPerLane + k];
-    int above = 0;  // pairs with larger keys: the chunks of lanes above this one
-    for (int l = 31; l > 0; --l) {
-      const int v = __shfl_sync(0xffffffffu, chunk, l);
-      if (l > lane) above += v;
+#pragma unroll
+    for (int k = 0; k < kPerLane / 4; ++k) {
+      const int4 h = reinterpret_cast<const int4*>(hist + chunk_lo)[k];
+      chunk += (h.x + h.y) + (h.z + h.w);
     }
+    // pairs in the chunks of lower lanes (larger keys): exclusive prefix sum
+    int incl = chunk;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(full, incl, d);
+      if (lane >= d) incl += v;
+    }
+    const unsigned own = __ballot_sync(full, pair_pos >= incl - chunk && pair_pos < incl);
+    const int o = own ? __ffs(own) - 1 : 0;
+    const int before_o = __shfl_sync(full, incl - chunk, o);
+    // inside chunk o, lane l takes keys hi = top - 2l and hi - 1 (descending)
+    const int hi = kTcCostKeys - 1 - kPerLane * o - 2 * lane;
+    const int h0 = hist[hi], h1 = hist[hi - 1];
+    int incl2 = h0 + h1;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(full, incl2, d);
+      if (lane >= d) incl2 += v;
+    }
+    const int first = before_o + incl2 - (h0 + h1);  // pairs before key hi
     int key = -1, rank = 0;
-    if (pair_pos >= above && pair_pos < above + chunk) {
-      int acc = above;
-      for (int k = kPerLane - 1; k >= 0; --k) {
-        const int h = hist[lane * kPerLane + k];
-        if (pair_pos < acc + h) {
-          key = lane * kPerLane + k;
-          rank = pair_pos - acc;
-          break;
-        }
-        acc += h;
-      }
+    if (pair_pos >= first && pair_pos < first + h0) {
+      key = hi;
+      rank = pair_pos - first;
+    } else if (pair_pos >= first + h0 && pair_pos < first + h0 + h1) {
+      key = hi - 1;
+      rank = pair_pos - first - h0;
     }
-    const unsigned owner = __ballot_sync(0xffffffffu, key >= 0);
+    const unsigned owner = __ballot_sync(full, key >= 0);
     const int src = owner ? __ffs(owner) - 1 : 0;
-    key = __shfl_sync(0xffffffffu, key, src);
-    rank = __shfl_sync(0xffffffffu, rank, src);
+    key = __shfl_sync(full, key, src);
+    rank = __shfl_sync(full, rank, src);
     // the rank-th pair (in id order) whose cost key is `key`
     int found = 0;
     for (int base = 0; base < pairs; base += 32) {
       const int id = base + lane;
-      const bool hit = id < pairs &&
-                       tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq) == key;
-      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      int c = -1;
+      if (id < pairs)
+        c = id < kTcCachedPairs ? cost[id]
+                                : tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq);
+      const unsigned m = __ballot_sync(full, c == key);
       const int n = __popc(m);
       if (rank < n) {
         unsigned mm = m;
@@ -178,17 +214,51 @@ __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, 
       rank -= n;
     }
     if (lane == 0) {
-      scratch[kTcCostKeys] = found;
-      scratch[kTcCostKeys + 1] = pos % p.num_kv_heads;
+      result[0] = found;
+      result[1] = pos % p.num_kv_heads;
     }
   }
   __syncthreads();
-  const int pair = scratch[kTcCostKeys];
-  kvh = scratch[kTcCostKeys + 1];
+  const int pair = result[0];
+  kvh = result[1];
   s = pair / p.blocks_per_seq;
   rb = pair % p.blocks_per_seq;
   __syncthreads();  // scratch is reused as the Q tiles
 }
+
+// Page ids of the producer warp's 128-token KV tiles, read from the block
+// table four tiles at a time (one page slot per lane) and a group ahead of
+// use, so that no TMA issue waits on a dependent global load: lane l holds
+// the page of sub-tile l % 8 of tile 4g + l / 8 of group g, even and odd
+// groups in two registers. Indices past the sequence end read its last page.
+struct TilePages {
+  const int32_t* bt_row;
+  int max_page_idx, block_size, lane;
+  int even, odd;
+
+  __device__ __forceinline__ int fetch(int g) const {
+    const int tok = (g * 4 + (lane >> 3)) * kTcKv + (lane & 7) * kTileTokens;
+    return __ldg(bt_row + min(tok / block_size, max_page_idx));
+  }
+  __device__ __forceinline__ void init() {
+    even = fetch(0);
+    odd = fetch(1);
+  }
+  // Call before tile j's V load (the K loads run ahead, in tile j / 4 or
+  // later): group j / 4 - 1 is dead, so group j / 4 + 1 takes its register.
+  __device__ __forceinline__ void advance(int j) {
+    if (j < 4 || (j & 3) != 0) return;
+    const int g = j / 4 + 1;
+    if (g & 1)
+      odd = fetch(g);
+    else
+      even = fetch(g);
+  }
+  // Page of sub-tile `lane % 8` of tile j (warp-collective).
+  __device__ __forceinline__ int page(int j) const {
+    return __shfl_sync(0xffffffffu, ((j >> 2) & 1) ? odd : even, (j & 3) * 8 + (lane & 7));
+  }
+};
 
 template <typename T, bool kFp8>
 __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
@@ -214,6 +284,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   uint64_t* raw_full = bars + 18;   // [2] FP8 staging: TMA -> converter warps
   uint64_t* raw_empty = bars + 20;  // [2] FP8 staging: converter warps -> TMA
+  uint64_t* q_full = bars + 22;     // softmax warps (256 arrivals, Q staged) -> MMA
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,6 +331,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       mbar_init(smem_u32(&o_done[x]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
+    mbar_init(smem_u32(q_full), 2 * kTcRows);
     if (kFp8) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&raw_full[i]), 1);
@@ -272,6 +344,12 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
     tmem_relinquish();
   }
+
+  // Barriers and the TMEM address are visible after this; the producer
+  // starts streaming K/V while the softmax warps still stage Q.
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
 
   // ---- softmax warps: this thread's row and its Q into shared memory ----
   const int x_tile = warp >> 2;       // Q tile of a softmax warp (0 or 1)
@@ -300,11 +378,10 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       }
       *reinterpret_cast<uint4*>(qtile + (c >> 3) * kTcHalf + swz128(t, c & 7)) = v;
     }
+    // generic-proxy writes -> the MMAs' async-proxy reads, then hand off
     fence_proxy_async_smem();
+    mbar_arrive(smem_u32(q_full));
   }
-  tc_fence_before_sync();
-  __syncthreads();
-  tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   bool ok = true;
 
@@ -330,8 +407,10 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 
   if (warp == kTcProducerWarp && kFp8) {
     // ------------------------------------------------------- FP8 producer --
-    const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
     const int max_page_idx = (seq_len - 1) / p.block_size;
+    TilePages pages{p.block_tables + (int64_t)s * p.block_table_stride, max_page_idx,
+                    p.block_size, lane, 0, 0};
+    pages.init();
     const uint32_t raw0 = sbase + L::kRaw0;
     int issued = 0;
     for (int i = 0; i < n_items && ok; ++i) {
@@ -345,18 +424,15 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       bool is_v;
       int j;
       item_at(i, is_v, j);
+      if (is_v) pages.advance(j);
       const uint32_t bar = smem_u32(&raw_full[i & 1]);
       if (lane == 0) mbar_arrive_expect_tx(bar, kTcRawTileBytes);
       __syncwarp();
+      const int page = pages.page(j);
       if (lane < kTcKv / kTileTokens) {
         const int tok = j * kTcKv + lane * kTileTokens;
-        int pidx = tok / p.block_size;
-        int row = tok % p.block_size;
-        if (pidx > max_page_idx) {  // past the sequence end: any valid page, masked later
-          pidx = max_page_idx;
-          row = 0;
-        }
-        const int page = bt_row[pidx];
+        // past the sequence end: the last page (any valid one), masked later
+        const int row = tok / p.block_size > max_page_idx ? 0 : tok % p.block_size;
         if (page < 0 || page >= p.num_blocks)
           report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
         tma_load_4d(raw0 + (i & 1) * kTcRawTileBytes + lane * kFp8TileBytes,
@@ -421,8 +497,10 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     // Issue order K0, K1, then (V_j, K_{j+2}) for j = 0, 1, ...: K runs two
     // tiles ahead (its stage frees as soon as the S MMAs of a tile retire),
     // V one to two tiles ahead.
-    const int32_t* bt_row = p.block_tables + (int64_t)s * p.block_table_stride;
     const int max_page_idx = (seq_len - 1) / p.block_size;
+    TilePages pages{p.block_tables + (int64_t)s * p.block_table_stride, max_page_idx,
+                    p.block_size, lane, 0, 0};
+    pages.init();
     int issued_k = 0, issued_v = 0;
     auto load = [&](bool is_v, int j) -> bool {
       const int nst = is_v ? kTcVStages : kTcKStages;
@@ -435,15 +513,11 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       const uint32_t bar = smem_u32(is_v ? &v_full[st] : &k_full[st]);
       if (lane == 0) mbar_arrive_expect_tx(bar, kTcTileBytes);
       __syncwarp();
+      const int page = pages.page(j);
       if (lane < kTcKv / kTileTokens) {
         const int tok = j * kTcKv + lane * kTileTokens;
-        int pidx = tok / p.block_size;
-        int row = tok % p.block_size;
-        if (pidx > max_page_idx) {  // past the sequence end: any valid page, masked later
-          pidx = max_page_idx;
-          row = 0;
-        }
-        const int page = bt_row[pidx];
+        // past the sequence end: the last page (any valid one), masked later
+        const int row = tok / p.block_size > max_page_idx ? 0 : tok % p.block_size;
         if (page < 0 || page >= p.num_blocks)
           report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
         const uint32_t dst =
@@ -457,6 +531,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     };
     for (int j = 0; j < min(2, n_total) && ok; ++j) ok = load(false, j);
     for (int j = 0; j < n_total && ok; ++j) {
+      pages.advance(j);
       ok = load(true, j);
       if (ok && j + 2 < n_total) ok = load(false, j + 2);
     }
@@ -523,8 +598,9 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         }
         return true;
       };
-      // prologue: S of tile 0 for both Q tiles
-      if (!wait_k(0)) ok = false;
+      // prologue: S of tile 0 for both Q tiles, once Q is staged
+      if (!mbar_wait(smem_u32(q_full), 0)) ok = false;
+      if (ok && !wait_k(0)) ok = false;
       if (ok && n_a > 0) issue_s(0, 0);
       if (ok && n_b > 0) issue_s(1, 0);
       if (ok) umma_commit(smem_u32(&k_empty[0]));  // after every S of tile 0
