@@ -26,7 +26,9 @@
 //     keeps the tensor core on one tile's MMAs while the other warpgroup runs
 //     its softmax (ping-pong), and because MMAs of one thread complete in
 //     order, "S_X(j) done" also means "PV_X(j-1) done": the softmax may then
-//     rescale O_X and overwrite S_X with P_X without further waits.
+//     rescale O_X and overwrite S_X with P_X without further waits. P is
+//     handed over in two 64-token halves, so the first four PV MMAs run while
+//     the softmax still exponentiates the second half.
 //   * S = Q K^T with A = Q, B = K both K-major from shared memory. The softmax
 //     writes P (16-bit) over S in TMEM and O += P V reads A = P from tensor
 //     memory and B = V N-major straight from the TMA tile.
@@ -278,13 +280,14 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   uint64_t* v_full = bars + 6;     // [2] TMA -> MMA
   uint64_t* v_empty = bars + 8;    // [2] MMA (commit after the PV MMAs) -> TMA
   uint64_t* s_full = bars + 10;    // [2] per Q tile: MMA (commit) -> softmax
-  uint64_t* p_ready = bars + 12;   // [2] per Q tile: softmax (128 arrivals) -> MMA
+  uint64_t* p_ready = bars + 12;   // [2] per Q tile: P tokens 0-63 written (128 arrivals) -> MMA
   uint64_t* o_done = bars + 14;    // [2] per Q tile: MMA (commit) -> epilogue
   uint64_t* mma_drain = bars + 16; // MMA (commit) -> MMA, before TMEM is freed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   uint64_t* raw_full = bars + 18;   // [2] FP8 staging: TMA -> converter warps
   uint64_t* raw_empty = bars + 20;  // [2] FP8 staging: converter warps -> TMA
   uint64_t* q_full = bars + 22;     // softmax warps (256 arrivals, Q staged) -> MMA
+  uint64_t* p_ready_hi = bars + 23; // [2] per Q tile: P tokens 64-127 written -> MMA
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     for (int x = 0; x < kTcTiles; ++x) {
       mbar_init(smem_u32(&s_full[x]), 1);
       mbar_init(smem_u32(&p_ready[x]), kTcRows);
+      mbar_init(smem_u32(&p_ready_hi[x]), kTcRows);
       mbar_init(smem_u32(&o_done[x]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
@@ -560,27 +564,29 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
                    k > 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[x]));
       };
-      auto issue_pv = [&](int x, int j) {
+      // PV k-steps [k0, k0 + 4): the 64 KV tokens of one half of P
+      auto issue_pv = [&](int x, int j, int k0) {
         const uint32_t vbase = sbase + kTcV0 + (j % kTcVStages) * kTcTileBytes;
         const uint32_t tP = tmem_base + x * 256;  // P (16-bit, packed) over S
 #pragma unroll
-        for (int k = 0; k < kTcKv / 16; ++k)
+        for (int k = k0; k < k0 + kTcKv / 32; ++k)
           umma_f16_ts(tmem_base + x * 256 + 128, tP + k * 8,
                       smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
                       (j > 0 || k > 0) ? 1u : 0u);
       };
+      // K/V tiles arrive through the async proxy (TMA, or the FP8 converters'
+      // proxy fence before their arrival): the mbarrier wait alone orders the
+      // MMAs' shared-memory reads after them, no tcgen05 fence.
       int k_ready = -1, v_ready = -1;  // highest tiles whose full phase was observed
       auto wait_k = [&](int j) {
         if (j <= k_ready) return true;
         if (!mbar_wait(smem_u32(&k_full[j % kTcKStages]), (j / kTcKStages) & 1)) return false;
-        tc_fence_after_sync();
         k_ready = j;
         return true;
       };
       auto wait_v = [&](int j) {
         if (j <= v_ready) return true;
         if (!mbar_wait(smem_u32(&v_full[j % kTcVStages]), (j / kTcVStages) & 1)) return false;
-        tc_fence_after_sync();
         v_ready = j;
         return true;
       };
@@ -590,7 +596,10 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         if (!mbar_wait(smem_u32(&p_ready[x]), j & 1)) return false;
         tc_fence_after_sync();
         if (!wait_v(j)) return false;
-        issue_pv(x, j);
+        issue_pv(x, j, 0);
+        if (!mbar_wait(smem_u32(&p_ready_hi[x]), j & 1)) return false;
+        tc_fence_after_sync();
+        issue_pv(x, j, kTcKv / 32);
         if (j == n_x - 1) umma_commit(smem_u32(&o_done[x]));
         if (j + 1 < n_x) {
           if (!wait_k(j + 1)) return false;
@@ -676,37 +685,8 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         m_used = m_tile;
         rescale = true;
       }
-      const float neg_base = m_used == kNegInf ? 0.f : -m_used;
-      // exponent arguments and row sums two columns at a time (f32x2)
-      const uint64_t scale2 = f2(scale, scale), base2 = f2(neg_base, neg_base);
-      uint64_t sk2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float sv[32];
-        tmem_ld32(tS + c * 32, sv);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0, x1;
-          f2_split(f2_fma(f2(sv[2 * i], sv[2 * i + 1]), scale2, base2), x0, x1);
-          float p0 = ex2_approx(x0);
-          float p1 = ex2_approx(x1);
-          if (need_mask) {
-            p0 = c * 32 + 2 * i < lim ? p0 : 0.f;
-            p1 = c * 32 + 2 * i + 1 < lim ? p1 : 0.f;
-          }
-          sk2[i & 1] = f2_add(sk2[i & 1], f2(p0, p1));
-          pk[i] = pack2<M>(p0, p1);
-        }
-        // P over S: chunk c's 32 values -> 16 columns at 16c, which only
-        // overlap S columns this row has already read
-        tmem_st16(tS + c * 16, pk);
-      }
-      float s0, s1, s2, s3;
-      f2_split(sk2[0], s0, s1);
-      f2_split(sk2[1], s2, s3);
-      const float sum = (s0 + s1) + (s2 + s3);
-      l = l * alpha + sum;
+      // O_X is stable (S_X(j) done implies PV_X(j-1) done): rescale it before
+      // any of P_X(j) is handed to the PV MMAs.
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -736,9 +716,43 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
         }
         fence_proxy_async_smem();
       }
-      tmem_wait_st();
-      tc_fence_before_sync();
-      mbar_arrive(smem_u32(&p_ready[x_tile]));
+      const float neg_base = m_used == kNegInf ? 0.f : -m_used;
+      // exponent arguments and row sums two columns at a time (f32x2); each
+      // 64-token half of P is handed to the MMA warp as soon as it is written
+      const uint64_t scale2 = f2(scale, scale), base2 = f2(neg_base, neg_base);
+      uint64_t sk2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld32(tS + c * 32, sv);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0, x1;
+          f2_split(f2_fma(f2(sv[2 * i], sv[2 * i + 1]), scale2, base2), x0, x1);
+          float p0 = ex2_approx(x0);
+          float p1 = ex2_approx(x1);
+          if (need_mask) {
+            p0 = c * 32 + 2 * i < lim ? p0 : 0.f;
+            p1 = c * 32 + 2 * i + 1 < lim ? p1 : 0.f;
+          }
+          sk2[i & 1] = f2_add(sk2[i & 1], f2(p0, p1));
+          pk[i] = pack2<M>(p0, p1);
+        }
+        // P over S: chunk c's 32 values -> 16 columns at 16c, which only
+        // overlap S columns this row has already read
+        tmem_st16(tS + c * 16, pk);
+        if (c == 1 || c == 3) {
+          tmem_wait_st();
+          tc_fence_before_sync();
+          mbar_arrive(smem_u32(c == 1 ? &p_ready[x_tile] : &p_ready_hi[x_tile]));
+        }
+      }
+      float s0, s1, s2, s3;
+      f2_split(sk2[0], s0, s1);
+      f2_split(sk2[1], s2, s3);
+      const float sum = (s0 + s1) + (s2 + s3);
+      l = l * alpha + sum;
     }
     if (ok && my_tiles > 0) {
       const bool done = mbar_wait(smem_u32(&o_done[x_tile]), 0);
