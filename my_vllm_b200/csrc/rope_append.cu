@@ -74,8 +74,11 @@ __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
 // cos/sin values stay in registers across its Hq + 2 Hkv rows, the two norm
 // weights in shared memory; the mean of squares is reduced over the group's
 // 8 lanes. Each group loads kRowsInFlight rows before computing any, so
-// every warp keeps 4 KiB of loads in flight.
-constexpr int kRowsInFlight = 4;  // rows each lane group loads before computing
+// every warp keeps 2 KiB of loads in flight; three 8-warp blocks per SM (24
+// warps, register-limited) keep more in flight per SM than two blocks with
+// batches of four rows.
+constexpr int kRowsInFlight = 2;  // rows each lane group loads before computing
+constexpr int kRopeCtasPerSm = 3;
 
 // FP8 E4M3 cache rows: 8 values of T (4 words) -> 8 bytes, each
 // e4m3(x * inv) with inv = 1 / scale rounded once to fp32, round to nearest even and
@@ -102,7 +105,7 @@ __device__ __forceinline__ uint2 quantize8(const uint32_t (&w)[4], float inv) {
 }
 
 template <typename T, bool kFp8>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, kRopeCtasPerSm)
     qk_norm_rope_append_kernel(const RopeAppendParams p) {
   using P = Pair<T>;
   // cache element type: T, or one byte (E4M3) per element
@@ -246,10 +249,10 @@ __global__ void __launch_bounds__(256, 2)
 
 cudaError_t launch_qk_norm_rope_append(const RopeAppendParams& p, int dtype, bool fp8_cache,
                                        cudaStream_t stream) {
-  // 8 warps per block, one token per warp; at most the 2 blocks per SM that
+  // 8 warps per block, one token per warp; at most the 3 blocks per SM that
   // fit at once, the grid-stride loop covers the rest
   int64_t blocks = (p.num_tokens + 7) / 8;
-  if (blocks > 148 * 2) blocks = 148 * 2;
+  if (blocks > 148 * kRopeCtasPerSm) blocks = 148 * kRopeCtasPerSm;
   if (blocks < 1) blocks = 1;
   if (dtype == B200_DTYPE_BFLOAT16) {
     if (fp8_cache)
