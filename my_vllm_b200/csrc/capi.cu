@@ -128,6 +128,56 @@ int cache_tensor_map(const void* base, const b200_paged_cache& c, CUtensorMap* o
   return B200_OK;
 }
 
+// Tensor map over q (16-bit) viewed as (head_dim, q head, token), 128-byte
+// swizzle; box = 64 elements x group heads x 128 / group tokens, i.e. one
+// d-half of a prefill Q tile's 128 (token, head) rows in row order.
+int q_tensor_map(const void* q, int dtype, int num_q_heads, int num_tokens,
+                 int64_t q_head_stride, int64_t q_token_stride, int group, CUtensorMap* out) {
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.ptr = reinterpret_cast<uint64_t>(q);
+  key.dims[0] = b200::kHeadDim;
+  key.dims[1] = num_q_heads;
+  key.dims[2] = num_tokens;
+  key.dims[3] = group;
+  key.strides[0] = q_head_stride;
+  key.strides[1] = q_token_stride;
+  key.dtype = 1000 + dtype;  // never equal to a cache map's key
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    auto it = map_cache().find(key);
+    if (it != map_cache().end()) {
+      *out = it->second;
+      return B200_OK;
+    }
+  }
+  auto fn = encode_fn();
+  if (fn == nullptr)
+    return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[3] = {(cuuint64_t)b200::kHeadDim, (cuuint64_t)num_q_heads,
+                              (cuuint64_t)num_tokens};
+  const cuuint64_t strides[2] = {(cuuint64_t)q_head_stride * 2, (cuuint64_t)q_token_stride * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)(128 / group)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType type = dtype == B200_DTYPE_BFLOAT16
+                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap m;
+  CUresult r = fn(&m, type, 3, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled (q) failed with CUresult " +
+                                   std::to_string(static_cast<int>(r)));
+  {
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    if (map_cache().size() > 4096) map_cache().clear();
+    map_cache().emplace(key, m);
+  }
+  *out = m;
+  return B200_OK;
+}
+
 int validate_cache(const b200_paged_cache* c) {
   if (c == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "cache descriptor is NULL");
   if (c->k_cache == nullptr || c->v_cache == nullptr)
@@ -545,7 +595,17 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.k_scale = cache->k_scale;
   p.v_scale = cache->v_scale;
   p.status = status;
-  cudaError_t e = b200::launch_paged_prefill_tc(mk, mv, p, cache->dtype, cache->kv_fp8 != 0,
+  // Q by TMA when its rows fit the box layout: 16-bit cache (the FP8 kernel
+  // converts Q while staging it) and a GQA group that divides 128.
+  CUtensorMap mq;
+  std::memset(&mq, 0, sizeof(mq));
+  p.q_tma = (cache->kv_fp8 == 0 && 128 % group == 0) ? 1 : 0;
+  if (p.q_tma && q_tensor_map(q, cache->dtype, num_q_heads, num_q_tokens, q_head_stride,
+                              q_token_stride, group, &mq) != B200_OK) {
+    p.q_tma = 0;  // strides the driver does not accept: the softmax warps stage Q
+    g_last_error.clear();
+  }
+  cudaError_t e = b200::launch_paged_prefill_tc(mk, mv, mq, p, cache->dtype, cache->kv_fp8 != 0,
                                                 cache->num_kv_heads, num_seqs, max_q_len,
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged prefill launch");

@@ -266,6 +266,7 @@ template <typename T, bool kFp8>
 __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                             const __grid_constant__ CUtensorMap tmap_v,
+                            const __grid_constant__ CUtensorMap tmap_q,
                             const PrefillParams p) {
   using L = TcLayout<kFp8>;
   using M = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   uint64_t* raw_full = bars + 18;   // [2] FP8 staging: TMA -> converter warps
   uint64_t* raw_empty = bars + 20;  // [2] FP8 staging: converter warps -> TMA
-  uint64_t* q_full = bars + 22;     // softmax warps (256 arrivals, Q staged) -> MMA
+  uint64_t* q_full = bars + 22;     // Q staged (TMA bytes, or 256 softmax arrivals) -> MMA
   uint64_t* p_ready_hi = bars + 23; // [2] per Q tile: P tokens 64-127 written -> MMA
 
   const int warp = threadIdx.x >> 5;
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       mbar_init(smem_u32(&o_done[x]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
-    mbar_init(smem_u32(q_full), 2 * kTcRows);
+    mbar_init(smem_u32(q_full), p.q_tma ? 1 : 2 * kTcRows);
     if (kFp8) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&raw_full[i]), 1);
@@ -360,13 +361,15 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   const int t = threadIdx.x & 127;    // row within the Q tile = TMEM lane
   int row_token = -1, row_head = 0, qpos = -1;
   if (warp < 8) {
-    const int r = x_tile * kTcRows + t;
+    const int r = x_tile * kTcRows + t;  // rows are (token, q head of the group) pairs
     const int tl = r / group;
     if (tl < tpc && tok_begin + tl < q_len) {
       row_token = tok_begin + tl;
       row_head = kvh * group + (r - tl * group);
       qpos = ctx + row_token;
     }
+  }
+  if (warp < 8 && !p.q_tma) {
     const uint4* src = reinterpret_cast<const uint4*>(
         reinterpret_cast<const T*>(p.q) + (int64_t)(q_start + max(row_token, 0)) * p.q_token_stride +
         (int64_t)row_head * p.q_head_stride);
@@ -533,6 +536,18 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       if (is_v) issued_v = j + 1; else issued_k = j + 1;
       return true;
     };
+    if (p.q_tma && lane == 0) {
+      // Q: per tile and d half one box of group heads x 128 / group tokens,
+      // which is the tile's 128 (token, head) rows in order; tokens past the
+      // query's end load the next sequence's rows or zeros, never written out.
+      const int tpt = kTcRows / group;
+      mbar_arrive_expect_tx(smem_u32(q_full), kTcTiles * kTcTileBytes);
+      for (int x = 0; x < kTcTiles; ++x)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sbase + kTcQ + x * kTcTileBytes + h * kTcHalf, &tmap_q, smem_u32(q_full),
+                      h * 64, kvh * group, q_start + tok_begin + x * tpt);
+    }
+    __syncwarp();
     for (int j = 0; j < min(2, n_total) && ok; ++j) ok = load(false, j);
     for (int j = 0; j < n_total && ok; ++j) {
       pages.advance(j);
@@ -795,6 +810,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 
 template <typename T, bool kFp8>
 static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
+                                   const CUtensorMap& mq,
                                    const PrefillParams& p, int num_kv_heads, int num_seqs,
                                    int max_q_len, cudaStream_t stream) {
   auto kernel = paged_prefill_tc_kernel<T, kFp8>;
@@ -810,22 +826,23 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   q.blocks_per_seq = blocks;
   const int64_t units = (int64_t)blocks * num_kv_heads * num_seqs;
   if (units > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, q);
+  kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, mq, q);
   return cudaGetLastError();
 }
 
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
+                                    const CUtensorMap& mq,
                                     const PrefillParams& p, int dtype, bool kv_fp8,
                                     int num_kv_heads, int num_seqs, int max_q_len,
                                     cudaStream_t stream) {
   if (dtype == B200_DTYPE_BFLOAT16)
-    return kv_fp8 ? launch_tc_typed<__nv_bfloat16, true>(mk, mv, p, num_kv_heads, num_seqs,
+    return kv_fp8 ? launch_tc_typed<__nv_bfloat16, true>(mk, mv, mq, p, num_kv_heads, num_seqs,
                                                          max_q_len, stream)
-                  : launch_tc_typed<__nv_bfloat16, false>(mk, mv, p, num_kv_heads, num_seqs,
+                  : launch_tc_typed<__nv_bfloat16, false>(mk, mv, mq, p, num_kv_heads, num_seqs,
                                                           max_q_len, stream);
-  return kv_fp8 ? launch_tc_typed<__half, true>(mk, mv, p, num_kv_heads, num_seqs, max_q_len,
+  return kv_fp8 ? launch_tc_typed<__half, true>(mk, mv, mq, p, num_kv_heads, num_seqs, max_q_len,
                                                 stream)
-                : launch_tc_typed<__half, false>(mk, mv, p, num_kv_heads, num_seqs, max_q_len,
+                : launch_tc_typed<__half, false>(mk, mv, mq, p, num_kv_heads, num_seqs, max_q_len,
                                                  stream);
 }
 
