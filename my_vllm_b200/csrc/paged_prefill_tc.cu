@@ -12,9 +12,11 @@
 //     form two UMMA M = 128 tiles, A and B, that share every K/V tile.
 //   * warps 0-3 / 4-7: two softmax warpgroups, one per Q tile; thread t of a
 //     group owns row t = TMEM lane t, so row max and row sum need no shuffles.
-//     They stage their Q tile into shared memory (K-major, 128-byte swizzle)
-//     and hand it to the MMA warp through an mbarrier, while the producer
-//     already streams K and V.
+//     Q reaches shared memory (K-major, 128-byte swizzle) by TMA, issued by
+//     the producer before its first K tile, when the cache is 16-bit and the
+//     GQA group divides 128 (then a tile's rows are one box of the q tensor);
+//     otherwise these warps stage it. Either way an mbarrier hands it to the
+//     MMA warp, and K/V streaming does not wait for it.
 //   * warp 8: TMA producer streaming 128-token K and V tiles of the paged
 //     cache (8 x 16-token sub-tiles, one lane each; page ids read from the
 //     block table four tiles at a time, a group ahead) into separate rings: K
