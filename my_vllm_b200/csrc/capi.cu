@@ -595,11 +595,11 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.k_scale = cache->k_scale;
   p.v_scale = cache->v_scale;
   p.status = status;
-  // Q by TMA when its rows fit the box layout: 16-bit cache (the FP8 kernel
-  // converts Q while staging it) and a GQA group that divides 128.
+  // Q by TMA when a tile's rows are one box of the q tensor: a GQA group that
+  // divides 128 (FP8 caches convert the landed Q to fp16 in shared memory).
   CUtensorMap mq;
   std::memset(&mq, 0, sizeof(mq));
-  p.q_tma = (cache->kv_fp8 == 0 && 128 % group == 0) ? 1 : 0;
+  p.q_tma = 128 % group == 0 ? 1 : 0;
   if (p.q_tma && q_tensor_map(q, cache->dtype, num_q_heads, num_q_tokens, q_head_stride,
                               q_token_stride, group, &mq) != B200_OK) {
     p.q_tma = 0;  // strides the driver does not accept: the softmax warps stage Q

@@ -28,8 +28,8 @@ struct PrefillParams {
   int num_seqs;
   int num_kv_heads;
   int blocks_per_seq;  // row blocks of the longest query chunk
-  int q_tma;           // 1: Q arrives by TMA through the q tensor map (16-bit caches,
-                       // group divides 128); 0: the softmax warps stage it
+  int q_tma;           // 1: Q arrives by TMA through the q tensor map (group divides
+                       // 128); 0: the softmax warps stage it
   int32_t* status;
 };
 

@@ -13,10 +13,11 @@
 //   * warps 0-3 / 4-7: two softmax warpgroups, one per Q tile; thread t of a
 //     group owns row t = TMEM lane t, so row max and row sum need no shuffles.
 //     Q reaches shared memory (K-major, 128-byte swizzle) by TMA, issued by
-//     the producer before its first K tile, when the cache is 16-bit and the
-//     GQA group divides 128 (then a tile's rows are one box of the q tensor);
-//     otherwise these warps stage it. Either way an mbarrier hands it to the
-//     MMA warp, and K/V streaming does not wait for it.
+//     the producer before its first K tile, when the GQA group divides 128
+//     (then a tile's rows are one box of the q tensor; FP8 caches convert
+//     the landed rows to fp16 in place); otherwise these warps stage it.
+//     Either way an mbarrier hands it to the MMA warp, and K/V streaming
+//     does not wait for it.
 //   * warp 8: TMA producer streaming 128-token K and V tiles of the paged
 //     cache (8 x 16-token sub-tiles, one lane each; page ids read from the
 //     block table four tiles at a time, a group ahead) into separate rings: K
@@ -47,7 +48,7 @@
 //     V tile as 16 KiB of FP8 into a 2-slot staging ring (one tile ahead)
 //     and converts it, exactly, into the same fp16 K-major / N-major tile
 //     layout the MMAs read (E4M3 values are all representable in fp16), then
-//     signals the tile full. Q is staged as fp16 and P packed as fp16, so the
+//     signals the tile full. Q is converted to fp16 and P packed as fp16, so the
 //     MMAs run kind::f16 on fp16 operands; the K scale folds into the softmax
 //     scale and the V scale into the final normalisation. The K ring has 2
 //     stages instead of 3 to make room for the staging ring.
@@ -291,6 +292,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   uint64_t* raw_empty = bars + 20;  // [2] FP8 staging: converter warps -> TMA
   uint64_t* q_full = bars + 22;     // Q staged (TMA bytes, or 256 softmax arrivals) -> MMA
   uint64_t* p_ready_hi = bars + 23; // [2] per Q tile: P tokens 64-127 written -> MMA
+  uint64_t* q_raw = bars + 25;      // FP8 caches: 16-bit Q landed by TMA -> softmax warps
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -338,7 +340,10 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       mbar_init(smem_u32(&o_done[x]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
-    mbar_init(smem_u32(q_full), p.q_tma ? 1 : 2 * kTcRows);
+    // 16-bit caches: the Q TMA bytes complete q_full; FP8 caches: the softmax
+    // warps' 256 arrivals do, after converting (a TMA-landed) Q to fp16
+    mbar_init(smem_u32(q_full), (p.q_tma && !kFp8) ? 1 : 2 * kTcRows);
+    mbar_init(smem_u32(q_raw), 1);
     if (kFp8) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&raw_full[i]), 1);
@@ -370,6 +375,25 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       row_head = kvh * group + (r - tl * group);
       qpos = ctx + row_token;
     }
+  }
+  if (kFp8 && warp < 8 && p.q_tma) {
+    // FP8 caches run the MMAs on fp16 operands: convert this row of the
+    // TMA-landed 16-bit Q in place (same size, same swizzled positions)
+    if (!mbar_wait(smem_u32(q_raw), 0) && lane == 0)
+      report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+    uint8_t* qtile = smem + kTcQ + x_tile * 2 * kTcHalf;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4* ptr = reinterpret_cast<uint4*>(qtile + (c >> 3) * kTcHalf + swz128(t, c & 7));
+      uint4 v = *ptr;
+      v.x = pair_to_f16(v.x, T());
+      v.y = pair_to_f16(v.y, T());
+      v.z = pair_to_f16(v.z, T());
+      v.w = pair_to_f16(v.w, T());
+      *ptr = v;
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(smem_u32(q_full));
   }
   if (warp < 8 && !p.q_tma) {
     const uint4* src = reinterpret_cast<const uint4*>(
@@ -414,8 +438,22 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   };
   const int n_items = 2 * n_total;
 
+  // Q by TMA (producer lane 0): per tile and d half one box of group heads x
+  // 128 / group tokens, which is the tile's 128 (token, head) rows in order;
+  // tokens past the query's end load the next sequence's rows or zeros, and
+  // those rows are never written out.
+  auto load_q = [&](uint64_t* bar) {
+    const int tpt = kTcRows / group;
+    mbar_arrive_expect_tx(smem_u32(bar), kTcTiles * kTcTileBytes);
+    for (int x = 0; x < kTcTiles; ++x)
+      for (int h = 0; h < 2; ++h)
+        tma_load_3d(sbase + kTcQ + x * kTcTileBytes + h * kTcHalf, &tmap_q, smem_u32(bar),
+                    h * 64, kvh * group, q_start + tok_begin + x * tpt);
+  };
   if (warp == kTcProducerWarp && kFp8) {
     // ------------------------------------------------------- FP8 producer --
+    if (p.q_tma && lane == 0) load_q(q_raw);
+    __syncwarp();
     const int max_page_idx = (seq_len - 1) / p.block_size;
     TilePages pages{p.block_tables + (int64_t)s * p.block_table_stride, max_page_idx,
                     p.block_size, lane, 0, 0};
@@ -538,17 +576,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       if (is_v) issued_v = j + 1; else issued_k = j + 1;
       return true;
     };
-    if (p.q_tma && lane == 0) {
-      // Q: per tile and d half one box of group heads x 128 / group tokens,
-      // which is the tile's 128 (token, head) rows in order; tokens past the
-      // query's end load the next sequence's rows or zeros, never written out.
-      const int tpt = kTcRows / group;
-      mbar_arrive_expect_tx(smem_u32(q_full), kTcTiles * kTcTileBytes);
-      for (int x = 0; x < kTcTiles; ++x)
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sbase + kTcQ + x * kTcTileBytes + h * kTcHalf, &tmap_q, smem_u32(q_full),
-                      h * 64, kvh * group, q_start + tok_begin + x * tpt);
-    }
+    if (p.q_tma && lane == 0) load_q(q_full);
     __syncwarp();
     for (int j = 0; j < min(2, n_total) && ok; ++j) ok = load(false, j);
     for (int j = 0; j < n_total && ok; ++j) {
