@@ -132,7 +132,11 @@ __device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int r
 // Pair costs kept in shared memory by tc_decode_unit (beyond this many pairs
 // the rank search recomputes them from the metadata).
 constexpr int kTcCachedPairs = 8192;
-constexpr int kTcScratchInts = kTcCostKeys + 4 + kTcCachedPairs;
+// The histogram is padded by 4 ints after every 64 keys, so the 32 lanes that
+// each sum one 64-key chunk with 16-byte loads spread over the banks.
+constexpr int kTcHistInts = kTcCostKeys + kTcCostKeys / 16;
+__device__ __forceinline__ int tc_hist_slot(int key) { return key + (key >> 6) * 4; }
+constexpr int kTcScratchInts = kTcHistInts + 4 + kTcCachedPairs;
 static_assert(kTcScratchInts * 4 <= kTcTiles * 2 * kTcHalf, "scratch lives in the Q tiles");
 
 // (sequence, row block, KV head) of grid position `pos`; `scratch` holds
@@ -141,17 +145,17 @@ static_assert(kTcScratchInts * 4 <= kTcTiles * 2 * kTcHalf, "scratch lives in th
 // shuffles only: the whole CTA waits on this before any load is issued.
 __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, int* scratch,
                                                int& s, int& rb, int& kvh) {
-  int* hist = scratch;                        // [kTcCostKeys]
-  int* result = scratch + kTcCostKeys;        // [2]
-  int* cost = scratch + kTcCostKeys + 4;      // [kTcCachedPairs]
+  int* hist = scratch;                        // [kTcHistInts], key k at tc_hist_slot(k)
+  int* result = scratch + kTcHistInts;        // [2]
+  int* cost = scratch + kTcHistInts + 4;      // [kTcCachedPairs]
   const int pairs = p.num_seqs * p.blocks_per_seq;
-  for (int i = threadIdx.x; i < kTcCostKeys / 4; i += blockDim.x)
+  for (int i = threadIdx.x; i < kTcHistInts / 4; i += blockDim.x)
     reinterpret_cast<int4*>(hist)[i] = make_int4(0, 0, 0, 0);
   __syncthreads();
   for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
     const int c = tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq);
     if (i < kTcCachedPairs) cost[i] = c;
-    atomicAdd(&hist[c], 1);
+    atomicAdd(&hist[tc_hist_slot(c)], 1);
   }
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -165,7 +169,7 @@ __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, 
     int chunk = 0;
 #pragma unroll
     for (int k = 0; k < kPerLane / 4; ++k) {
-      const int4 h = reinterpret_cast<const int4*>(hist + chunk_lo)[k];
+      const int4 h = reinterpret_cast<const int4*>(hist + tc_hist_slot(chunk_lo))[k];
       chunk += (h.x + h.y) + (h.z + h.w);
     }
     // pairs in the chunks of lower lanes (larger keys): exclusive prefix sum
@@ -180,7 +184,7 @@ __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, 
     const int before_o = __shfl_sync(full, incl - chunk, o);
     // inside chunk o, lane l takes keys hi = top - 2l and hi - 1 (descending)
     const int hi = kTcCostKeys - 1 - kPerLane * o - 2 * lane;
-    const int h0 = hist[hi], h1 = hist[hi - 1];
+    const int h0 = hist[tc_hist_slot(hi)], h1 = hist[tc_hist_slot(hi - 1)];
     int incl2 = h0 + h1;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -811,11 +815,17 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       T* orow = reinterpret_cast<T*>(p.out) +
                 (int64_t)(q_start + max(row_token, 0)) * p.out_token_stride +
                 (int64_t)row_head * p.out_head_stride;
+      // the row's 128 O columns in four loads under one wait (the softmax
+      // registers are free by now)
+      uint32_t ob[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tO + c * 32, ov);
-        if (row_token >= 0) {
+      for (int c = 0; c < 4; ++c) tmem_ld32_issue(tO + c * 32, ob[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_wait_ld32(ob[c]);
+      if (row_token >= 0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float* ov = reinterpret_cast<const float*>(ob[c]);
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
             uint4 pk;
