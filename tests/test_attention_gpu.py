@@ -325,3 +325,29 @@ def test_decode_and_prefill_group_and_block_shapes(cuda_device, hq, hkv, bs):
     torch.cuda.synchronize()
     expected, rows = sample_oracle(w, list(range(len(q_lens))))
     assert_close_to_oracle(out[rows], expected, w.q.dtype)
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (12, 4)])
+def test_prefill_q_view_of_fused_qkv(cuda_device, hq, hkv):
+    """The engine's q is a view into the fused qkv projection (token stride
+    (Hq + 2 Hkv) x D): the prefill must read it through those strides, for a
+    GQA group that takes Q by TMA (4) and one that stages it per thread (3).
+    Same values as a contiguous q, so the outputs are identical."""
+    q_lens = [200, 1, 64, 513]
+    kv_lens = [700, 33, 64, 2100]
+    w = workloads.small_case(q_lens, kv_lens, len(q_lens), Hq=hq, Hkv=hkv, device=cuda_device)
+    T, D = w.q.shape[0], w.q.shape[2]
+    qkv = torch.zeros(T, (hq + 2 * hkv) * D, dtype=w.q.dtype, device=cuda_device)
+    qkv[:, : hq * D] = w.q.reshape(T, hq * D)
+    q_view = qkv[:, : hq * D].view(T, hq, D)
+    assert q_view.stride(0) == (hq + 2 * hkv) * D
+    outs = []
+    for q in (w.q, q_view):
+        out = torch.full_like(w.q, float("nan"))
+        ops.paged_prefill(q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens,
+                          w.query_start_loc, out, max(q_lens), 128 ** -0.5)
+        torch.cuda.synchronize()
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    expected, rows = sample_oracle(w, list(range(len(q_lens))))
+    assert_close_to_oracle(outs[1][rows], expected, w.q.dtype)
