@@ -289,6 +289,8 @@ B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_seq_stride,
  * positions < seq_len - q_len + i + 1 (bottom-right causal mask,
  * tests/test_attention_backend.py:686-693).
  * max_q_len bounds the chunk length (host value from the metadata).
+ * num_q_tokens is the number of rows q holds: Q tiles may be fetched as whole
+ * boxes through a tensor map bounded by it, so it must not exceed q's rows.
  * Replaces BatchPrefillWithPagedKVCacheWrapper.run as called from
  * FlashInferBackend.forward (attention_backend.py:992-994, 1014-1019).
  */
