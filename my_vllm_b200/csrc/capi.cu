@@ -128,7 +128,7 @@ int cache_tensor_map(const void* base, const b200_paged_cache& c, CUtensorMap* o
   return B200_OK;
 }
 
-// Tensor map over q (16-bit) viewed as (head_dim, q head, token), 128-byte
+// Tensor map over q or out (16-bit) viewed as (head_dim, q head, token), 128-byte
 // swizzle; box = 64 elements x group heads x 128 / group tokens, i.e. one
 // d-half of a prefill Q tile's 128 (token, head) rows in row order.
 int q_tensor_map(const void* q, int dtype, int num_q_heads, int num_tokens,
@@ -605,7 +605,17 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
     p.q_tma = 0;  // strides the driver does not accept: the softmax warps stage Q
     g_last_error.clear();
   }
-  cudaError_t e = b200::launch_paged_prefill_tc(mk, mv, mq, p, cache->dtype, cache->kv_fp8 != 0,
+  // Whole output tiles leave by TMA stores under the same condition.
+  CUtensorMap mo;
+  std::memset(&mo, 0, sizeof(mo));
+  p.o_tma = 128 % group == 0 ? 1 : 0;
+  if (p.o_tma && q_tensor_map(out, cache->dtype, num_q_heads, num_q_tokens, out_head_stride,
+                              out_token_stride, group, &mo) != B200_OK) {
+    p.o_tma = 0;  // per-thread stores
+    g_last_error.clear();
+  }
+  cudaError_t e = b200::launch_paged_prefill_tc(mk, mv, mq, mo, p, cache->dtype,
+                                                cache->kv_fp8 != 0,
                                                 cache->num_kv_heads, num_seqs, max_q_len,
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged prefill launch");

@@ -30,16 +30,19 @@ struct PrefillParams {
   int blocks_per_seq;  // row blocks of the longest query chunk
   int q_tma;           // 1: Q arrives by TMA through the q tensor map (group divides
                        // 128); 0: the softmax warps stage it
+  int o_tma;           // 1: Q tiles whose rows all belong to the sequence leave by a
+                       // TMA store through the out tensor map; 0: per-thread stores
   int32_t* status;
 };
 
 // tcgen05 / TMEM prefill: 128 packed (query token, q head of the group) rows
 // per CTA on UMMA M = 128 tiles, so the GQA heads of a KV head share every
 // K/V tile the CTA loads.
-// mq: tensor map over q viewed as (head_dim, q head, token), box 64 x group x
-// 128 / group, 128-byte swizzle; read only when p.q_tma is set.
+// mq / mo: tensor maps over q / out viewed as (head_dim, q head, token), box
+// 64 x group x 128 / group, 128-byte swizzle; used only when p.q_tma / p.o_tma
+// is set.
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
-                                    const CUtensorMap& mq,
+                                    const CUtensorMap& mq, const CUtensorMap& mo,
                                     const PrefillParams& p, int dtype, bool kv_fp8,
                                     int num_kv_heads, int num_seqs, int max_q_len,
                                     cudaStream_t stream);

@@ -38,6 +38,9 @@
 //   * Online softmax in the exp2 domain with a lazy rescale: the running
 //     maximum only moves when a tile's maximum exceeds it by more than 2^8, so
 //     O (in TMEM) is rarely rescaled; O / l is independent of that choice.
+//   * Epilogue: O / l packed to T; a tile whose rows all belong to the
+//     sequence is written into its freed Q region and stored by TMA, other
+//     tiles row by row.
 //   * The bottom-right causal mask and the sequence end are applied in
 //     registers; V rows past the sequence end are zeroed in shared memory
 //     before the last PV MMAs (never-written cache slots may hold NaN).
@@ -274,6 +277,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                             const __grid_constant__ CUtensorMap tmap_v,
                             const __grid_constant__ CUtensorMap tmap_q,
+                            const __grid_constant__ CUtensorMap tmap_o,
                             const PrefillParams p) {
   using L = TcLayout<kFp8>;
   using M = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
@@ -297,6 +301,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   uint64_t* q_full = bars + 22;     // Q staged (TMA bytes, or 256 softmax arrivals) -> MMA
   uint64_t* p_ready_hi = bars + 23; // [2] per Q tile: P tokens 64-127 written -> MMA
   uint64_t* q_raw = bars + 25;      // FP8 caches: 16-bit Q landed by TMA -> softmax warps
+  uint64_t* o_staged = bars + 26;   // [2] per Q tile (128 arrivals): output rows in smem
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -348,6 +353,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
     // warps' 256 arrivals do, after converting (a TMA-landed) Q to fp16
     mbar_init(smem_u32(q_full), (p.q_tma && !kFp8) ? 1 : 2 * kTcRows);
     mbar_init(smem_u32(q_raw), 1);
+    for (int x = 0; x < kTcTiles; ++x) mbar_init(smem_u32(&o_staged[x]), kTcRows);
     if (kFp8) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(smem_u32(&raw_full[i]), 1);
@@ -822,7 +828,15 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
       for (int c = 0; c < 4; ++c) tmem_ld32_issue(tO + c * 32, ob[c]);
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_wait_ld32(ob[c]);
-      if (row_token >= 0) {
+      // A tile whose 128 rows all belong to the sequence (group divides 128)
+      // is one box of the out tensor: its rows go to the tile's Q region
+      // (free: every MMA of this tile has completed) in the 128-byte swizzled
+      // layout, and one thread stores the box with TMA. Other tiles, whose
+      // trailing rows would fall on the next sequence, store row by row.
+      const int tpt = kTcRows / group;
+      const bool box_out = p.o_tma && tok_begin + (x_tile + 1) * tpt <= q_len;
+      uint8_t* otile = smem + kTcQ + x_tile * kTcTileBytes;
+      if (box_out || row_token >= 0) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const float* ov = reinterpret_cast<const float*>(ob[c]);
@@ -833,7 +847,26 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
             pk.y = pack2<T>(ov[q8 * 8 + 2] * inv_l, ov[q8 * 8 + 3] * inv_l);
             pk.z = pack2<T>(ov[q8 * 8 + 4] * inv_l, ov[q8 * 8 + 5] * inv_l);
             pk.w = pack2<T>(ov[q8 * 8 + 6] * inv_l, ov[q8 * 8 + 7] * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = pk;
+            const int chunk = c * 4 + q8;  // 16-byte chunk of the 256-byte row
+            if (box_out)
+              *reinterpret_cast<uint4*>(otile + (chunk >> 3) * kTcHalf + swz128(t, chunk & 7)) = pk;
+            else
+              *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = pk;
+          }
+        }
+      }
+      if (box_out) {
+        fence_proxy_async_smem();  // generic writes -> the TMA's async-proxy reads
+        mbar_arrive(smem_u32(&o_staged[x_tile]));
+        if (t == 0) {
+          if (mbar_wait(smem_u32(&o_staged[x_tile]), 0)) {
+            const int tok0 = q_start + tok_begin + x_tile * tpt;
+            tma_store_3d(&tmap_o, smem_u32(otile), 0, kvh * group, tok0);
+            tma_store_3d(&tmap_o, smem_u32(otile + kTcHalf), 64, kvh * group, tok0);
+            bulk_commit_group();
+            bulk_wait_group_all();  // shared memory is read and out written before exit
+          } else {
+            report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
           }
         }
       }
@@ -850,7 +883,7 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 
 template <typename T, bool kFp8>
 static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
-                                   const CUtensorMap& mq,
+                                   const CUtensorMap& mq, const CUtensorMap& mo,
                                    const PrefillParams& p, int num_kv_heads, int num_seqs,
                                    int max_q_len, cudaStream_t stream) {
   auto kernel = paged_prefill_tc_kernel<T, kFp8>;
@@ -866,23 +899,23 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   q.blocks_per_seq = blocks;
   const int64_t units = (int64_t)blocks * num_kv_heads * num_seqs;
   if (units > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, mq, q);
+  kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, mq, mo, q);
   return cudaGetLastError();
 }
 
 cudaError_t launch_paged_prefill_tc(const CUtensorMap& mk, const CUtensorMap& mv,
-                                    const CUtensorMap& mq,
+                                    const CUtensorMap& mq, const CUtensorMap& mo,
                                     const PrefillParams& p, int dtype, bool kv_fp8,
                                     int num_kv_heads, int num_seqs, int max_q_len,
                                     cudaStream_t stream) {
   if (dtype == B200_DTYPE_BFLOAT16)
-    return kv_fp8 ? launch_tc_typed<__nv_bfloat16, true>(mk, mv, mq, p, num_kv_heads, num_seqs,
+    return kv_fp8 ? launch_tc_typed<__nv_bfloat16, true>(mk, mv, mq, mo, p, num_kv_heads, num_seqs,
                                                          max_q_len, stream)
-                  : launch_tc_typed<__nv_bfloat16, false>(mk, mv, mq, p, num_kv_heads, num_seqs,
+                  : launch_tc_typed<__nv_bfloat16, false>(mk, mv, mq, mo, p, num_kv_heads, num_seqs,
                                                           max_q_len, stream);
-  return kv_fp8 ? launch_tc_typed<__half, true>(mk, mv, mq, p, num_kv_heads, num_seqs, max_q_len,
+  return kv_fp8 ? launch_tc_typed<__half, true>(mk, mv, mq, mo, p, num_kv_heads, num_seqs, max_q_len,
                                                 stream)
-                : launch_tc_typed<__half, false>(mk, mv, mq, p, num_kv_heads, num_seqs, max_q_len,
+                : launch_tc_typed<__half, false>(mk, mv, mq, mo, p, num_kv_heads, num_seqs, max_q_len,
                                                  stream);
 }
 
