@@ -13,8 +13,16 @@ heads [r*8/N, (r+1)*8/N) and their q heads, its own cache shard and the same
 block tables. There is no collective on the data path; ranks meet only at the
 timing barriers. `value` = algorithmic bytes of all ranks / max rank time.
 
-`--impl reference` times the reference's CPU semantics (the oracle port, all
-host threads) on a bounded sample of the same workload.
+`--impl reference` times the reference's own CPU implementation of the path —
+the unmodified engine installed in baseline/_ref: KVCacheStore.forward_native
+(nanovllm/layers/attention.py:69-85) and _paged_attention_reference
+(tests/test_attention_backend.py:660-699) — on the full config 2 batch, with
+all host threads, on rank 0 only.
+
+The default line also carries sub-records measured after the headline on the
+same GPU (N = 1 only), each with its own roofline: config 3's mixed step and
+its prefill kernel, config 5 at block sizes 16 and 256, a 4 x 8192-token
+causal prefill, and the plain KV append at 65,536 rows.
 """
 
 from __future__ import annotations
@@ -35,6 +43,7 @@ REPO = Path(__file__).resolve().parent
 METRIC = "paged decode attn+KV-append HBM GB/s and tokens/s at 1/2/4/8 B200"
 TOTAL_Q_HEADS, TOTAL_KV_HEADS, HEAD_DIM, BLOCK_SIZE = 32, 8, 128, 16
 BATCH, CONTEXT = 256, 4096
+SEED_LONG_PREFILL, SEED_APPEND = 2026 + 7, 2026 + 8
 WORKLOAD = ("config2: Qwen3-8B decode step, one layer: KV append of 256 rows + paged GQA "
             "decode, B 256, ctx 4096, Hq 32 / Hkv 8, D 128, bs 16, bf16")
 
@@ -47,7 +56,10 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--cpu-sample-seqs", type=int, default=16)
+    ap.add_argument("--cpu-sample-seqs", type=int, default=32,
+                    help="sequences of the bounded CPU-baseline sample in the GPU arm")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="skip the config 3 / config 5 / prefill / append sub-records")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="smaller batches are for profiler captures only")
     ap.add_argument("--workload", choices=("config2", "config3", "config4", "rope_append"),
@@ -69,69 +81,120 @@ def parse_args():
 
 # ------------------------------------------------------------------ clocks --
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clock, max clock, power and throttle reasons of the ranks' GPUs,
+    sampled through NVML every millisecond on a background thread (ctypes
+    releases the GIL during each call), so a timed region of a few
+    milliseconds still holds several samples. Falls back to a 200 ms
+    ``nvidia-smi`` loop where NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_indices):
-        self.gpus = set(gpu_indices)
-        self.rows = []
-        self.proc = None
-        self.thread = None
+    def __init__(self, gpu_indices, period_s=0.001):
+        self.gpus = list(gpu_indices)
+        self.period = period_s
+        self.samples = []  # (time, gpu, sm_mhz, sm_max_mhz, power_w, reasons)
         self.window = None
+        self.source = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [(g, pynvml.nvmlDeviceGetHandleByIndex(g)) for g in self.gpus]
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            max_sm = {g: pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                      for g, h in handles}
+        except Exception:  # no NVML: nvidia-smi at its 200 ms minimum
+            self._start_smi()
+            return
+        self.source = f"NVML every {self.period * 1e3:g} ms"
+
+        def loop():
+            while not self._stop.is_set():
+                now = time.time()
+                for g, h in handles:
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        bits = get_reasons(h)
+                        power = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    except Exception:
+                        continue
+                    reasons = [n for n, b in self.REASON_BITS.items() if bits & b]
+                    self.samples.append((now, g, float(sm), float(max_sm[g]), power, reasons))
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+
+    def _start_smi(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self.proc = None
+            self._proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
+        self.source = "nvidia-smi every 200 ms"
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append((time.time(), [c.strip() for c in line.split(",")]))
+        def read():
+            for line in self._proc.stdout:
+                r = [c.strip() for c in line.split(",")]
+                if len(r) < 9 or not r[0].isdigit() or int(r[0]) not in self.gpus:
+                    continue
+                try:
+                    sm, smax = float(r[1]), float(r[2])
+                except ValueError:
+                    continue
+                power = float(r[3]) if r[3].replace(".", "").isdigit() else 0.0
+                reasons = [n for n, v in zip(names, r[5:9]) if v.lower() == "active"]
+                self.samples.append((time.time(), int(r[0]), sm, smax, power, reasons))
+
+        self._thread = threading.Thread(target=read, daemon=True)
+        self._thread.start()
 
     def mark(self, t0, t1):
         self.window = (t0, t1)
 
     def stop(self):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=5)
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        rows = [(t, r) for t, r in self.rows if len(r) >= 9 and r[0].isdigit()
-                and int(r[0]) in self.gpus]
-        in_window = rows
+        rows = list(self.samples)
         note = "during the timed region"
         if self.window is not None:
             t0, t1 = self.window
-            inside = [(t, r) for t, r in rows if t0 - 0.2 <= t <= t1 + 0.2]
+            inside = [r for r in rows if t0 <= r[0] <= t1]
             if inside:
-                in_window = inside
+                rows = inside
             else:
-                note = "around the timed region (shorter than the 200 ms sampling period)"
-        if not in_window:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sm = [float(r[1]) for _, r in in_window if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for _, r in in_window if r[2].replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({name for _, r in in_window for name, v in zip(names, r[5:9])
-                          if v.strip().lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
-                "samples": len(in_window), "when": note}
+                note = "around the timed region (no sample inside it)"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": self.source}
+        sm = [r[2] for r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
+                "sm_max_mhz": max(r[3] for r in rows),
+                "power_w_max": round(max(r[4] for r in rows), 1),
+                "reasons": sorted({n for r in rows for n in r[5]}),
+                "samples": len(rows), "when": note, "source": self.source}
 
 
 def physical_gpu_indices(world):
@@ -145,7 +208,7 @@ def physical_gpu_indices(world):
 
 # ---------------------------------------------------------------- workload --
 def make_shard(rank, world, device, batch=BATCH):
-    from my_vllm_b200 import workloads
+    import workloads
 
     if TOTAL_KV_HEADS % world:
         raise SystemExit(f"--gpus must divide {TOTAL_KV_HEADS} (KV heads are sharded)")
@@ -174,17 +237,65 @@ def committed_traffic():
 
 
 # ------------------------------------------------------------ CPU baseline --
+def reference_cpu_path():
+    """The reference's own CPU implementation of the path, from the unmodified
+    engine installed in baseline/_ref: ``KVCacheStore.forward_native``
+    (nanovllm/layers/attention.py:69-85, selected by platform "cpu") and the
+    fp32 ``_paged_attention_reference`` of its test suite
+    (tests/test_attention_backend.py:660-699). None where it is not installed."""
+    from baseline import install_ref
+
+    if not install_ref.add_to_path():
+        return None
+    from nanovllm.layers.attention import KVCacheStore
+    from nanovllm.layers.custom_op import CustomOpConfig
+    from test_attention_backend import _paged_attention_reference
+
+    return KVCacheStore(CustomOpConfig(platform="cpu")), _paged_attention_reference
+
+
 def cpu_sample(num_seqs, seed=7):
-    """A bounded CPU-resident sample of config 2: `num_seqs` sequences of
-    4096 tokens with their own pages (same heads, dtype and layout)."""
-    from my_vllm_b200 import workloads
+    """A CPU-resident config 2 batch of `num_seqs` sequences of 4096 tokens
+    (all 256 = the full workload), same heads, dtype and layout."""
+    import workloads
 
     return workloads.config2(device="cpu", seed=seed, batch=num_seqs, ctx=CONTEXT)
 
 
+def reference_csr(w):
+    """kv_indptr / page_indices from the dense tables, as the engine's
+    FlashInferBackend.build_metadata builds them for trusted metadata
+    (attention_backend.py:700-713); the reference attention takes this CSR."""
+    offsets = [0]
+    for count in w.block_counts:
+        offsets.append(offsets[-1] + count)
+    kv_indptr = torch.tensor(offsets, dtype=torch.int32)
+    page_indices = torch.cat(tuple(w.block_tables[row, :count]
+                                   for row, count in enumerate(w.block_counts))).contiguous()
+    return kv_indptr, page_indices
+
+
+def make_reference_step(w):
+    """One step of the reference's CPU path over workload `w`: the append of
+    the new rows, then attention of every sequence. Returns (step, kind)."""
+    path = reference_cpu_path()
+    if path is not None:
+        store, attend = path
+        kv_indptr, page_indices = reference_csr(w)
+        q_lens = tuple([1] * w.num_seqs)
+        kv_lens = tuple(w.extra["seq_lens_host"])
+
+        def step():
+            store(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+            attend(w.q, w.k_cache, w.v_cache, kv_indptr, page_indices, q_lens, kv_lens)
+
+        return step, "reference"
+    return (lambda: time_oracle(w, os.cpu_count() or 1)), "port"
+
+
 def time_oracle(w, threads):
-    """Run the oracle's append + attention over the sample on `threads`
-    host threads (sequences split across them); returns seconds."""
+    """The oracle port of the same two steps (used only where the reference
+    engine is not installed): sequences split across `threads` host threads."""
     from concurrent.futures import ThreadPoolExecutor
 
     import numpy as np
@@ -207,65 +318,67 @@ def time_oracle(w, threads):
 
     def run(ids):
         idx = np.array(ids)
-        sub_tables = tables[idx]
-        indptr, pages = oracle.block_tables_to_csr(sub_tables, lens[idx], w.block_size)
+        indptr, pages = oracle.block_tables_to_csr(tables[idx], lens[idx], w.block_size)
         return oracle.paged_attention(q[idx], k_cache, v_cache, indptr, pages, [1] * len(ids),
                                       lens[idx].tolist(), dtype="bfloat16")
 
-    try:
-        from threadpoolctl import threadpool_limits
-        limiter = threadpool_limits(limits=1)
-    except ImportError:  # pragma: no cover
-        limiter = None
-    t0 = time.perf_counter()
     oracle.kv_append(key, value, k_cache, v_cache, slots)
     with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
         list(pool.map(run, chunks))
-    dt = time.perf_counter() - t0
-    if limiter is not None:
-        limiter.unregister() if hasattr(limiter, "unregister") else None
-    return dt
 
 
 def cpu_baseline_leg(sample_seqs):
-    threads = os.cpu_count() or 1
+    """The reference's CPU path on a bounded sample (about 10 s of CPU work)."""
+    torch.set_num_threads(os.cpu_count() or 1)
     w = cpu_sample(sample_seqs)
     bytes_per_run = w.kv_bytes_read() + w.append_bytes()
-    time_oracle(w, threads)  # warm
+    step, kind = make_reference_step(w)
+    step()  # warm
     runs, elapsed = 0, 0.0
     while elapsed < 10.0 and runs < 500:
-        elapsed += time_oracle(w, threads)
+        t0 = time.perf_counter()
+        step()
+        elapsed += time.perf_counter() - t0
         runs += 1
     gbs = bytes_per_run * runs / elapsed / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+    what = ("the reference's KVCacheStore.forward_native + _paged_attention_reference"
+            if kind == "reference" else "the numpy oracle port")
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": kind,
             "sample": f"{sample_seqs} of the 256 sequences (ctx 4096, 8 KV heads), append + "
-                      f"decode through the numpy oracle, {runs} runs in {elapsed:.1f} s"}
+                      f"decode through {what}, {runs} runs in {elapsed:.1f} s"}
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's own CPU path on the FULL config 2
+    batch (256 sequences x 4096 tokens) every step, all host threads."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    w = cpu_sample(args.cpu_sample_seqs)
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = cpu_sample(BATCH, seed=7)
     bytes_per_step = w.kv_bytes_read() + w.append_bytes()
+    step, kind = make_reference_step(w)
     for _ in range(args.warmup):
-        time_oracle(w, threads)
+        step()
     total = 0.0
     for _ in range(args.steps):
-        total += time_oracle(w, threads)
+        t0 = time.perf_counter()
+        step()
+        total += time.perf_counter() - t0
     gbs = bytes_per_step * args.steps / total / 1e9
+    what = ("KVCacheStore.forward_native + _paged_attention_reference from the unmodified "
+            "engine (baseline/_ref)" if kind == "reference" else "numpy oracle port")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": CONTEXT,
-                   "parallelism": f"kv-head shards x{args.gpus}",
-                   "sample_per_step": f"{args.cpu_sample_seqs} sequences"},
-        "tokens_per_s": round(args.cpu_sample_seqs * args.steps / total, 2),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"{args.cpu_sample_seqs} of 256 sequences per step"},
+                   "parallelism": "host CPU, rank 0 only"},
+        "tokens_per_s": round(BATCH * args.steps / total, 2),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s",
+                         "cores": torch.get_num_threads(), "kind": kind,
+                         "sample": f"the full batch (256 sequences) every step, {what}"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -288,7 +401,7 @@ def run_ours(args, rank, world, local_rank):
     w = make_shard(rank, world, device, args.batch)
     fp8 = args.kv_dtype == "fp8"
     if fp8:
-        from my_vllm_b200 import workloads
+        import workloads
 
         w.k_cache = workloads.to_fp8_cache(w.k_cache, 1.0)
         w.v_cache = workloads.to_fp8_cache(w.v_cache, 1.0)
@@ -503,6 +616,9 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
+    extra = {}
+    if world == 1 and not fp8 and not args.no_subrecords and args.batch == BATCH:
+        extra = subrecords(device, min(args.steps, 50), args.warmup)
 
     ms_per_step = elapsed_ms / args.steps
     total_bytes = step_bytes * world
@@ -565,6 +681,7 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = cpu
     if sampler is not None:
         line["clocks"] = sampler.summary()
+    line.update(extra)
     print(json.dumps(line), flush=True)
 
 
@@ -573,16 +690,43 @@ def visible_pairs(q_len, kv_len):
     return q_len * (kv_len - q_len) + q_len * (q_len + 1) // 2
 
 
-def run_config3(args):
+def tensor_peak():
+    try:
+        peaks_data = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(peaks_data["bf16_tflops"]), "measured burst cuBLAS bf16 (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def event_ms(fn, steps, warmup, stream, between=None):
+    """Average device time of `fn` per call (CUDA events on `stream` around
+    every call); `between` runs untimed before each call (an L2 flush)."""
+    for _ in range(max(3, warmup)):
+        if between is not None:
+            between()
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for a, b in ev:
+        if between is not None:
+            between()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+
+def measure_config3(device, steps, warmup, fp8=False):
     """Config 3 (mixed chunked prefill + decode) on one GPU: the step is the
     engine's MIXED route — append 2172 rows, prefill rows [0, 2048) on the
-    tcgen05 kernel, decode rows [2048, 2172) — timed per kernel."""
-    from my_vllm_b200 import B200PagedBackend, ops, workloads
+    tcgen05 kernel, decode rows [2048, 2172) — and each kernel timed on its own
+    (back to back, so the decode's 2 GB stream separates prefill launches)."""
+    import workloads
+    from my_vllm_b200 import B200PagedBackend, ops
 
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
     w = workloads.config3(device=device)
-    fp8 = args.kv_dtype == "fp8"
     scales = {}
     if fp8:
         w.k_cache = workloads.to_fp8_cache(w.k_cache, 1.0)
@@ -621,29 +765,29 @@ def run_config3(args):
         ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
         backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     torch.cuda.synchronize()
     s0 = torch.cuda.Event(enable_timing=True)
     s1 = torch.cuda.Event(enable_timing=True)
     s0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     s1.record(stream)
     torch.cuda.synchronize()
-    step_ms = s0.elapsed_time(s1) / args.steps
+    step_ms = s0.elapsed_time(s1) / steps
 
     # per-kernel rooflines: the same kernels launched back to back on one stream
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
         prefill()
         decode()
     torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
         ev[i][0].record(stream)
         prefill()
@@ -653,41 +797,163 @@ def run_config3(args):
         ev[i][3].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
-    serial_ms = t0.elapsed_time(t1) / args.steps
-    ms = step_ms
-    pre_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
-    dec_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
-    try:
-        peaks_data = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
-        tflops_peak, src = float(peaks_data["bf16_tflops"]), "measured burst cuBLAS bf16"
-    except (OSError, KeyError, ValueError):
-        tflops_peak, src = 1590.0, "fallback"
+    backend.check_status()
+    serial_ms = t0.elapsed_time(t1) / steps
+    pre_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / steps
+    dec_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / steps
+    tflops_peak, src = tensor_peak()
     hbm, hbm_src = peaks()
     pre_tf = flops / (pre_ms * 1e-3) / 1e12
     dec_gbs = decode_kv_bytes / (dec_ms * 1e-3) / 1e9
-    line = {
-        "metric": METRIC + " (config 3 mixed step)", "value": round(step_bytes / (ms * 1e-3) / 1e9, 2),
-        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
-        "ms_per_step": round(ms, 5), "serial_ms_per_step": round(serial_ms, 5),
-        "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 (KV cache fp8-e4m3)" if fp8 else "bf16",
-        "data": "synthetic",
-        "config": {"workload": "config3: 4 x 512-token prefill chunks on shared prefix hits "
-                               "0/512/1024/2048 + 124 decode rows ctx U[128, 8192], Qwen3-8B "
-                               "heads, bs 16; append 2172 rows"
-                               + ("; KV pool FP8 E4M3" if fp8 else ""),
-                   "l2": "decode streams 2.1 GB per step between prefill launches"},
+    return {
+        "workload": "config3: 4 x 512-token prefill chunks on shared prefix hits "
+                    "0/512/1024/2048 + 124 decode rows ctx U[128, 8192], Qwen3-8B heads, bs 16; "
+                    "append 2172 rows" + ("; KV pool FP8 E4M3" if fp8 else ""),
+        "value": round(step_bytes / (step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "ms_per_step": round(step_ms, 5), "serial_ms_per_step": round(serial_ms, 5),
+        "steps": steps,
         "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel",
                      "achieved": round(dec_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(dec_gbs / hbm, 4), "launch_ms": round(dec_ms, 5),
+                     "frac": round(dec_gbs / hbm, 4), "peak_source": f"{hbm_src} hbm_gbs",
+                     "launch_ms": round(dec_ms, 5),
                      "algorithmic_bytes_per_launch": decode_kv_bytes},
         "roofline_prefill": {"bound": "tensor", "kernel": "paged_prefill_tc_kernel",
                              "achieved": round(pre_tf, 1), "peak": tflops_peak,
                              "unit": "TFLOP/s", "frac": round(pre_tf / tflops_peak, 4),
                              "peak_source": src, "launch_ms": round(pre_ms, 5),
                              "algorithmic_flops_per_launch": flops},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 3 * steps,
     }
+
+
+def measure_config5(device, block_size, steps, warmup):
+    """Config 5: long-context split-KV decode, B 32 x 32768 tokens (4 GiB of
+    KV per step), Qwen3-8B heads, at block size 16 or 256."""
+    import workloads
+    from my_vllm_b200 import B200PagedBackend, ops
+
+    w = workloads.config5(device=device, block_size=block_size)
+    backend = B200PagedBackend(w.num_q_heads, w.num_kv_heads, HEAD_DIM, block_size,
+                               torch.bfloat16)
+    plan = backend.build_plan(w.common_metadata())
+    stream = torch.cuda.current_stream(device)
+    ops.store_kvcache(w.key, w.value, w.k_cache, w.v_cache, w.slot_mapping)
+    ms = event_ms(lambda: backend.forward(w.q, w.key, w.value, w.k_cache, w.v_cache, plan),
+                  steps, warmup, stream)
+    backend.check_status()
+    hbm, src = peaks()
+    kv = w.kv_bytes_read()
+    gbs = kv / (ms * 1e-3) / 1e9
+    parts = plan.metadata.decode_plan.num_parts
+    return {
+        "workload": f"config5: B 32, ctx 32768, Hq 32 / Hkv 8, D 128, bs {block_size}, bf16, "
+                    "split-KV decode + reduce",
+        "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5), "steps": steps,
+        "decode_split": parts,
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel + decode_reduce_kernel",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_source": f"{src} hbm_gbs",
+                     "launch_ms": round(ms, 5), "algorithmic_bytes_per_launch": kv},
+        "gpu_launches": (2 if parts > 1 else 1) * steps,
+    }
+
+
+def measure_prefill_long(device, steps, warmup, seqs=4, tokens=8192):
+    """Steady-state prefill rate: `seqs` fresh causal prefills of `tokens`
+    tokens each (no prefix), Qwen3-8B heads — long enough that per-CTA
+    set-up and the last wave's tail are small next to the steady state."""
+    import workloads
+    from my_vllm_b200 import ops
+
+    w = workloads.small_case([tokens] * seqs, [tokens] * seqs, seqs, Hq=32, Hkv=8,
+                             device=device, seed=SEED_LONG_PREFILL)
+    out = torch.empty_like(w.q)
+    stream = torch.cuda.current_stream(device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    ms = event_ms(lambda: ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables,
+                                            w.seq_lens, w.query_start_loc, out, tokens,
+                                            HEAD_DIM ** -0.5, status=status),
+                  steps, warmup, stream)
+    if int(status.item()):
+        raise RuntimeError(f"prefill reported status {int(status.item())}")
+    flops = seqs * 4 * 32 * HEAD_DIM * visible_pairs(tokens, tokens)
+    tf = flops / (ms * 1e-3) / 1e12
+    peak, src = tensor_peak()
+    return {
+        "workload": f"prefill_long: {seqs} x {tokens}-token causal prefill, no prefix, Hq 32 / "
+                    "Hkv 8, D 128, bs 16, bf16",
+        "value": round(tf, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 5), "steps": steps,
+        "roofline": {"bound": "tensor", "kernel": "paged_prefill_tc_kernel",
+                     "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tf / peak, 4), "peak_source": src,
+                     "launch_ms": round(ms, 5), "algorithmic_flops_per_launch": flops},
+        "gpu_launches": steps,
+    }
+
+
+def measure_append(device, steps, warmup, rows=65536):
+    """The plain KV append (store_kvcache) at a size where it is not
+    launch-bound: `rows` new K/V rows of Qwen3-8B (8 KV heads x 128, bf16)
+    scattered to random slots of a pool twice that size. Algorithmic bytes:
+    read the K and V rows, write them into the cache (2 x 2 x rows x 2 KiB)."""
+    from my_vllm_b200 import ops
+
+    g = torch.Generator(device=device).manual_seed(SEED_APPEND)
+    key = torch.randn(rows, TOTAL_KV_HEADS, HEAD_DIM, generator=g, device=device).bfloat16()
+    value = torch.randn_like(key)
+    blocks = 2 * rows // BLOCK_SIZE
+    k_cache = torch.zeros(blocks, BLOCK_SIZE, TOTAL_KV_HEADS, HEAD_DIM, dtype=torch.bfloat16,
+                          device=device)
+    v_cache = torch.zeros_like(k_cache)
+    slots = torch.randperm(blocks * BLOCK_SIZE, generator=g, device=device)[:rows].int()
+    stream = torch.cuda.current_stream(device)
+    ms = event_ms(lambda: ops.store_kvcache(key, value, k_cache, v_cache, slots), steps,
+                  warmup, stream)
+    row_bytes = TOTAL_KV_HEADS * HEAD_DIM * 2
+    alg = 2 * 2 * rows * row_bytes  # K and V, read + write
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, src = peaks()
+    return {
+        "workload": f"append_64k: {rows} K/V rows (8 KV heads x 128, bf16) to random slots of a "
+                    f"{blocks}-block pool",
+        "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5), "steps": steps,
+        "l2": f"{alg / 1e6:.0f} MB per launch (> 126 MB L2)",
+        "roofline": {"bound": "hbm", "kernel": "kv_append_kernel", "achieved": round(gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "peak_source": f"{src} hbm_gbs", "launch_ms": round(ms, 5),
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": steps,
+    }
+
+
+def subrecords(device, steps, warmup):
+    """The sub-records of the default line (each measured on its own, after
+    the headline, on the same GPU)."""
+    records = {}
+    for name, fn in (("config3", lambda: measure_config3(device, steps, warmup)),
+                     ("config5_bs16", lambda: measure_config5(device, 16, steps, warmup)),
+                     ("config5_bs256", lambda: measure_config5(device, 256, steps, warmup)),
+                     ("prefill_long", lambda: measure_prefill_long(device, steps, warmup)),
+                     ("append_64k", lambda: measure_append(device, steps, warmup))):
+        records[name] = fn()
+        torch.cuda.empty_cache()
+    return records
+
+
+def run_config3(args):
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rec = measure_config3(device, args.steps, args.warmup, fp8=args.kv_dtype == "fp8")
+    line = {"metric": METRIC + " (config 3 mixed step)", "value": rec["value"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": rec["ms_per_step"], "serial_ms_per_step": rec["serial_ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 (KV cache fp8-e4m3)" if args.kv_dtype == "fp8" else "bf16",
+            "data": "synthetic",
+            "config": {"workload": rec["workload"],
+                       "l2": "decode streams 2.1 GB per step between prefill launches"},
+            "roofline": rec["roofline"], "roofline_prefill": rec["roofline_prefill"],
+            "gpu_launches": rec["gpu_launches"]}
     print(json.dumps(line), flush=True)
 
 
@@ -700,7 +966,8 @@ def run_flashinfer_comparator(args):
     max-abs difference between the two outputs."""
     import flashinfer
 
-    from my_vllm_b200 import B200PagedBackend, workloads
+    import workloads
+    from my_vllm_b200 import B200PagedBackend
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -804,7 +1071,8 @@ def run_config4(args, rank, world, local_rank):
     the free HBM; below tp 4 the pool cannot hold every block and the block
     tables are sampled with replacement (stated in the line). value = KV +
     append bytes of all ranks / max rank step time; tokens/s = 512 / step."""
-    from my_vllm_b200 import B200PagedBackend, ops, workloads
+    import workloads
+    from my_vllm_b200 import B200PagedBackend, ops
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)

@@ -160,13 +160,36 @@ B200_API int b200_qk_norm_rope_append_fp8(
  * sits at KV position seq_lens[s] - q_len + (t - query_start_loc[s]) and is
  * stored in slot block_tables[s][pos / block_size] * block_size
  * + pos % block_size; a block-table entry of -1 (no cache) gives slot -1.
- * block_tables rows must hold ceil(seq_lens[s] / block_size) entries.
+ * max_blocks is the number of valid columns of block_tables (<= its row
+ * stride) and num_blocks the pool size: a position past a row's max_blocks
+ * columns, or a page id >= num_blocks, gives slot -1 and sets
+ * B200_STATUS_SLOT_OUT_OF_RANGE in *status (NULL = no report), so malformed
+ * metadata never reads past a table row.
  * slot_mapping: int32 [num_tokens] output.
  */
 B200_API int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride,
+                                     int32_t max_blocks, int64_t num_blocks,
                                      const int32_t* seq_lens, const int32_t* query_start_loc,
                                      int32_t num_seqs, int32_t num_tokens, int32_t block_size,
-                                     int32_t* slot_mapping, void* stream);
+                                     int32_t* slot_mapping, int32_t* status, void* stream);
+
+/*
+ * Padded block tables, built on the device from the per-sequence block lists.
+ * Replaces ModelRunner.prepare_block_tables
+ * (nanovllm/engine/model_runner.py:354-358), which pads every
+ * seq.block_table with -1 to the longest one on the host and copies the
+ * [num_seqs, max_len] table. Here the caller uploads the lists once, packed:
+ * block_ids int32 [offsets[num_seqs]] holds the lists back to back and
+ * offsets int32 [num_seqs + 1] their boundaries (offsets[0] = 0). Row s of
+ * block_tables (int32, row stride block_table_stride >= max_blocks) receives
+ * block_ids[offsets[s] .. offsets[s+1]) followed by -1 up to max_blocks
+ * columns. A list longer than max_blocks is cut there and reported with
+ * B200_STATUS_PAGE_OUT_OF_RANGE.
+ */
+B200_API int b200_build_block_tables(const int32_t* block_ids, const int32_t* offsets,
+                                     int32_t num_seqs, int32_t max_blocks,
+                                     int32_t* block_tables, int64_t block_table_stride,
+                                     int32_t* status, void* stream);
 
 /*
  * Paged KV cache description (NHD). Strides are in elements of the cache's
@@ -265,7 +288,11 @@ B200_API int b200_paged_decode(const void* q, int64_t q_seq_stride, int64_t q_he
  *     B200_ERR_INVALID_ARGUMENT before anything is launched.
  *   - The first call on a device looks up that device's scratch address
  *     (cudaGetSymbolAddress, with the device current); make that first call
- *     before any stream capture.
+ *     before any stream capture. The address is remembered per device and
+ *     per CUDA context: a call from another context on the same device (a
+ *     host with its own driver context, or the primary context recreated
+ *     after a device reset) looks it up again, so that call is again a
+ *     first call.
  *   - Every call on a device shares the one scratch array, which keeps the
  *     last call's contents. Calls that overlap on the GPU (other streams,
  *     other host threads) race on it: serialise them.
@@ -289,8 +316,9 @@ B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_seq_stride,
  * positions < seq_len - q_len + i + 1 (bottom-right causal mask,
  * tests/test_attention_backend.py:686-693).
  * max_q_len bounds the chunk length (host value from the metadata).
- * num_q_tokens is the number of rows q holds: Q tiles may be fetched as whole
- * boxes through a tensor map bounded by it, so it must not exceed q's rows.
+ * num_q_tokens is the number of rows q holds: Q tiles may be fetched, and
+ * output tiles stored, as whole boxes through tensor maps bounded by it, so
+ * both q and out must hold at least num_q_tokens rows.
  * Replaces BatchPrefillWithPagedKVCacheWrapper.run as called from
  * FlashInferBackend.forward (attention_backend.py:992-994, 1014-1019).
  */

@@ -29,7 +29,7 @@ DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
 DTYPE_FP8_E4M3 = 2
 
-ABI_VERSION = 201
+ABI_VERSION = 300
 
 # Size of the scratch array built into the library for
 # b200_paged_decode_noalloc (B200_NOALLOC_DECODE_SCRATCH_BYTES).
@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "b200_store_kvcache",
     "b200_store_kvcache_fp8",
     "b200_build_slot_mapping",
+    "b200_build_block_tables",
     "b200_qk_norm_rope_append",
     "b200_qk_norm_rope_append_fp8",
     "b200_paged_decode_plan",
@@ -100,7 +101,9 @@ _SIGNATURES = {
         [_VP, _I64, _VP, _I64, _I32, _VP, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _I64, _VP, _VP],
         _I32,
     ),
-    "b200_build_slot_mapping": ([_VP, _I64, _VP, _VP, _I32, _I32, _I32, _VP, _VP], _I32),
+    "b200_build_slot_mapping": (
+        [_VP, _I64, _I32, _I64, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP], _I32),
+    "b200_build_block_tables": ([_VP, _VP, _I32, _I32, _VP, _I64, _VP, _VP], _I32),
     "b200_qk_norm_rope_append": (
         [
             _VP, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _F32, _VP, _VP,

@@ -25,7 +25,6 @@ from types import MappingProxyType
 from typing import Any
 
 import torch
-import torch.nn.functional as F
 
 from . import _native, ops
 from .contract import (
@@ -35,6 +34,9 @@ from .contract import (
     AttentionRoute,
     BatchType,
     CommonAttentionMetadata,
+    _classify_batch,
+    _torch_sdpa_varlen,
+    _validate_common_metadata,
 )
 
 BACKEND_NAME = "b200"
@@ -79,108 +81,27 @@ class B200DecodeGraphState:
 
 
 def validate_common_metadata(common: CommonAttentionMetadata, *, require_cuda: bool) -> None:
-    """The engine's metadata contract (attention_backend.py:1384-1481).
+    """The engine's own metadata validator (attention_backend.py:1384-1481).
 
     Type and shape checks always run; value checks that need a device read run
     only for untrusted metadata, so a trusted plan never synchronises.
     """
-    if not isinstance(common, CommonAttentionMetadata):
-        raise TypeError("common must be CommonAttentionMetadata")
-    for name in ("num_prefill_seqs", "num_decode_seqs", "num_prefill_tokens",
-                 "num_decode_tokens", "max_q_len", "max_kv_len", "num_kv_blocks",
-                 "num_prefill_kv_blocks"):
-        value = getattr(common, name)
-        if isinstance(value, bool) or not isinstance(value, int):
-            raise TypeError(f"common.{name} must be an int")
-        if value < 0:
-            raise ValueError(f"common.{name} must be non-negative")
-    if common.num_seqs <= 0:
-        raise ValueError("attention metadata must contain at least one sequence")
-    if common.num_decode_tokens != common.num_decode_seqs:
-        raise ValueError("decode suffix must contain one query token per sequence")
-    if not isinstance(common.trusted, bool):
-        raise TypeError("common.trusted must be a bool")
-    for name in ("query_start_loc", "seq_lens", "slot_mapping"):
-        tensor = getattr(common, name)
-        if not isinstance(tensor, torch.Tensor):
-            raise TypeError(f"common.{name} must be a torch.Tensor")
-        if tensor.dtype != torch.int32:
-            raise TypeError(f"common.{name} must have dtype torch.int32")
-        if tensor.ndim != 1:
-            raise ValueError(f"common.{name} must be one-dimensional")
-        if require_cuda and tensor.device.type != "cuda":
-            raise ValueError(f"common.{name} must be on CUDA")
-    if common.query_start_loc.numel() != common.num_seqs + 1:
-        raise ValueError("query_start_loc length must equal number of sequences + 1")
-    if common.seq_lens.numel() != common.num_seqs:
-        raise ValueError("seq_lens length must equal number of sequences")
-    if common.slot_mapping.numel() != common.num_query_tokens:
-        raise ValueError("slot_mapping length must equal number of query tokens")
-    if not common.trusted:
-        if int(common.query_start_loc[0].item()) != 0:
-            raise ValueError("query_start_loc must start at zero")
-        if int(common.query_start_loc[-1].item()) != common.num_query_tokens:
-            raise ValueError("query_start_loc must end at num_query_tokens")
-        query_lengths = common.query_start_loc[1:] - common.query_start_loc[:-1]
-        if common.num_decode_seqs and not bool(
-            torch.all(query_lengths[common.num_prefill_seqs:] == 1).item()
-        ):
-            raise ValueError("every decode sequence must have one query token")
-        if not bool(torch.all(common.seq_lens > 0).item()):
-            raise ValueError("all KV sequence lengths must be positive")
-    block_tables = common.block_tables
-    if block_tables is not None:
-        if not isinstance(block_tables, torch.Tensor):
-            raise TypeError("common.block_tables must be a torch.Tensor")
-        if block_tables.dtype != torch.int32:
-            raise TypeError("common.block_tables must have dtype torch.int32")
-        if block_tables.ndim != 2:
-            raise ValueError("common.block_tables must be two-dimensional")
-        if block_tables.size(0) != common.num_seqs:
-            raise ValueError("block_tables row count must equal number of sequences")
-        if require_cuda and block_tables.device.type != "cuda":
-            raise ValueError("common.block_tables must be on CUDA")
+    _validate_common_metadata(common, require_cuda=require_cuda)
 
 
 def classify_batch(common: CommonAttentionMetadata) -> BatchType:
-    """Single batch classification point (attention_backend.py:1484-1491)."""
-    if common.num_prefill_seqs == 0:
-        if common.num_decode_seqs <= 0:
-            raise ValueError("pure decode batch must contain decode requests")
-        return BatchType.PURE_DECODE
-    if common.num_decode_seqs == 0:
-        return BatchType.PURE_PREFILL
-    return BatchType.MIXED
+    """The engine's single batch classification point (attention_backend.py:1484-1491)."""
+    return _classify_batch(common)
 
 
 def cacheless_varlen_attention(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, common: CommonAttentionMetadata
 ) -> torch.Tensor:
     """Causal attention without a cache for the engine's memory-sizing warmup
-    (the WARMUP route; the engine's own helper is attention_backend.py:1556-1624).
-    Runs once at start-up on the GPU, outside the serving hot path."""
-    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
-        raise ValueError("cacheless attention expects rank-3 Q/K/V")
-    if k.shape != v.shape:
-        raise ValueError("cacheless key and value shapes must match")
-    if q.size(0) != k.size(0):
-        raise ValueError("cacheless warmup requires matching query and KV token counts")
-    if q.size(1) % k.size(1):
-        raise ValueError("query head count must be divisible by KV head count")
-    boundaries = common.query_start_loc.cpu().tolist()
-    repeat = q.size(1) // k.size(1)
-    scale = 1.0 / (q.size(-1) ** 0.5)
-    outputs = []
-    for start, end in zip(boundaries[:-1], boundaries[1:]):
-        qs = q[start:end].transpose(0, 1).unsqueeze(0)
-        ks = k[start:end].transpose(0, 1).unsqueeze(0)
-        vs = v[start:end].transpose(0, 1).unsqueeze(0)
-        if repeat != 1:
-            ks = ks.repeat_interleave(repeat, dim=1)
-            vs = vs.repeat_interleave(repeat, dim=1)
-        out = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=scale)
-        outputs.append(out.squeeze(0).transpose(0, 1))
-    return torch.cat(outputs, dim=0) if outputs else torch.empty_like(q)
+    (the WARMUP route): the engine's own dependency-free helper
+    (attention_backend.py:1580-1624), run once at start-up on the GPU, outside
+    the serving hot path."""
+    return _torch_sdpa_varlen(q, k, v, common)
 
 
 class B200PagedBackend(AttentionBackend):

@@ -232,7 +232,7 @@ void set_last_error(const std::string& message) { g_last_error = message; }
 
 extern "C" {
 
-int b200_abi_version(void) { return 201; }
+int b200_abi_version(void) { return 300; }
 
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -373,21 +373,40 @@ int b200_qk_norm_rope_append_fp8(
 }
 
 int b200_build_slot_mapping(const int32_t* block_tables, int64_t block_table_stride,
-                            const int32_t* seq_lens, const int32_t* query_start_loc,
-                            int32_t num_seqs, int32_t num_tokens, int32_t block_size,
-                            int32_t* slot_mapping, void* stream) {
+                            int32_t max_blocks, int64_t num_blocks, const int32_t* seq_lens,
+                            const int32_t* query_start_loc, int32_t num_seqs,
+                            int32_t num_tokens, int32_t block_size, int32_t* slot_mapping,
+                            int32_t* status, void* stream) {
   g_last_error.clear();
-  if (num_seqs < 0 || num_tokens < 0 || block_size <= 0)
+  if (num_seqs < 0 || num_tokens < 0 || block_size <= 0 || max_blocks < 0 || num_blocks < 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "sizes must be non-negative, block_size positive");
   if (num_tokens == 0) return B200_OK;
   if (num_seqs == 0) return fail(B200_ERR_INVALID_ARGUMENT, "tokens without sequences");
   if (!block_tables || !seq_lens || !query_start_loc || !slot_mapping)
     return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
-  cudaError_t e = b200::launch_build_slot_mapping(block_tables, block_table_stride, seq_lens,
-                                                  query_start_loc, num_seqs, num_tokens,
-                                                  block_size, slot_mapping,
-                                                  static_cast<cudaStream_t>(stream));
+  if (max_blocks > block_table_stride)
+    return fail(B200_ERR_INVALID_ARGUMENT, "max_blocks exceeds the block-table row stride");
+  cudaError_t e = b200::launch_build_slot_mapping(
+      block_tables, block_table_stride, max_blocks, num_blocks, seq_lens, query_start_loc,
+      num_seqs, num_tokens, block_size, slot_mapping, status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "slot mapping launch");
+  return B200_OK;
+}
+
+int b200_build_block_tables(const int32_t* block_ids, const int32_t* offsets,
+                            int32_t num_seqs, int32_t max_blocks, int32_t* block_tables,
+                            int64_t block_table_stride, int32_t* status, void* stream) {
+  g_last_error.clear();
+  if (num_seqs < 0 || max_blocks < 0 || block_table_stride < max_blocks)
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "sizes must be non-negative and the row stride at least max_blocks");
+  if (num_seqs == 0 || max_blocks == 0) return B200_OK;
+  if (!block_ids || !offsets || !block_tables)
+    return fail(B200_ERR_INVALID_ARGUMENT, "NULL tensor pointer");
+  cudaError_t e = b200::launch_build_block_tables(block_ids, offsets, num_seqs, max_blocks,
+                                                  block_tables, block_table_stride, status,
+                                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "block table launch");
   return B200_OK;
 }
 

@@ -223,11 +223,15 @@ cudaError_t launch_kv_append_fp8(const void* key, int64_t key_row_stride, const 
 }
 
 // Slot of every new token, from the batch metadata (see b200_build_slot_mapping).
+// A position past the table row (pos / block_size >= max_blocks) or a page
+// id outside the pool gives slot -1 and sets B200_STATUS_SLOT_OUT_OF_RANGE.
 __global__ void __launch_bounds__(256)
     build_slot_mapping_kernel(const int32_t* __restrict__ block_tables, int64_t bt_stride,
+                              int max_blocks, int64_t num_blocks,
                               const int32_t* __restrict__ seq_lens,
                               const int32_t* __restrict__ query_start_loc, int num_seqs,
-                              int num_tokens, int block_size, int32_t* __restrict__ slots) {
+                              int num_tokens, int block_size, int32_t* __restrict__ slots,
+                              int32_t* status) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= num_tokens) return;
   // sequence s with query_start_loc[s] <= t < query_start_loc[s + 1]
@@ -243,21 +247,62 @@ __global__ void __launch_bounds__(256)
   const int pos = __ldg(seq_lens + s) - q_len + (t - q0);
   int32_t slot = -1;
   if (pos >= 0) {
-    const int32_t page = __ldg(block_tables + (int64_t)s * bt_stride + pos / block_size);
-    if (page >= 0) slot = page * block_size + pos % block_size;
+    const int col = pos / block_size;
+    if (col >= max_blocks) {
+      report_status(status, B200_STATUS_SLOT_OUT_OF_RANGE);
+    } else {
+      const int32_t page = __ldg(block_tables + (int64_t)s * bt_stride + col);
+      if (page >= (int64_t)num_blocks) report_status(status, B200_STATUS_SLOT_OUT_OF_RANGE);
+      else if (page >= 0) slot = page * block_size + pos % block_size;
+    }
   }
   slots[t] = slot;
 }
 
 cudaError_t launch_build_slot_mapping(const int32_t* block_tables, int64_t bt_stride,
+                                      int max_blocks, int64_t num_blocks,
                                       const int32_t* seq_lens, const int32_t* query_start_loc,
                                       int num_seqs, int num_tokens, int block_size,
-                                      int32_t* slots, cudaStream_t stream) {
+                                      int32_t* slots, int32_t* status, cudaStream_t stream) {
   const int threads = 256;
   const int blocks = (num_tokens + threads - 1) / threads;
   build_slot_mapping_kernel<<<blocks, threads, 0, stream>>>(
-      block_tables, bt_stride, seq_lens, query_start_loc, num_seqs, num_tokens, block_size,
-      slots);
+      block_tables, bt_stride, max_blocks, num_blocks, seq_lens, query_start_loc, num_seqs,
+      num_tokens, block_size, slots, status);
+  return cudaGetLastError();
+}
+
+// Padded block tables from the packed per-sequence block lists (see
+// b200_build_block_tables). One warp per row, lanes on consecutive columns:
+// every store is a coalesced 128-byte line, entries past the row's count are
+// -1. A row whose list is longer than the table is cut at max_blocks and
+// reported (B200_STATUS_PAGE_OUT_OF_RANGE).
+__global__ void __launch_bounds__(256)
+    build_block_tables_kernel(const int32_t* __restrict__ block_ids,
+                              const int32_t* __restrict__ offsets, int num_seqs,
+                              int max_blocks, int32_t* __restrict__ tables, int64_t stride,
+                              int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < num_seqs; row += warps) {
+    const int begin = __ldg(offsets + row);
+    const int count = __ldg(offsets + row + 1) - begin;
+    if (count > max_blocks && lane == 0) report_status(status, B200_STATUS_PAGE_OUT_OF_RANGE);
+    int32_t* dst = tables + (int64_t)row * stride;
+    for (int col = lane; col < max_blocks; col += 32)
+      dst[col] = col < count ? __ldg(block_ids + begin + col) : -1;
+  }
+}
+
+cudaError_t launch_build_block_tables(const int32_t* block_ids, const int32_t* offsets,
+                                      int num_seqs, int max_blocks, int32_t* tables,
+                                      int64_t stride, int32_t* status, cudaStream_t stream) {
+  const int threads = 256;
+  const int rows_per_block = threads / 32;
+  int blocks = (num_seqs + rows_per_block - 1) / rows_per_block;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  build_block_tables_kernel<<<blocks, threads, 0, stream>>>(block_ids, offsets, num_seqs,
+                                                            max_blocks, tables, stride, status);
   return cudaGetLastError();
 }
 

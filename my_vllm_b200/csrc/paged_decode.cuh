@@ -79,8 +79,13 @@ cudaError_t launch_kv_append_fp8(const void* key, int64_t key_row_stride, const 
                                  int64_t num_slots, int32_t* status, cudaStream_t stream);
 
 cudaError_t launch_build_slot_mapping(const int32_t* block_tables, int64_t bt_stride,
+                                      int max_blocks, int64_t num_blocks,
                                       const int32_t* seq_lens, const int32_t* query_start_loc,
                                       int num_seqs, int num_tokens, int block_size,
-                                      int32_t* slots, cudaStream_t stream);
+                                      int32_t* slots, int32_t* status, cudaStream_t stream);
+
+cudaError_t launch_build_block_tables(const int32_t* block_ids, const int32_t* offsets,
+                                      int num_seqs, int max_blocks, int32_t* tables,
+                                      int64_t stride, int32_t* status, cudaStream_t stream);
 
 }  // namespace b200

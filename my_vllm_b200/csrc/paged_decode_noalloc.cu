@@ -14,7 +14,13 @@
 // library holds that memory until the process exits. In host code the
 // array's name is only a host-side stand-in, never a device address, so the
 // address is fetched once per device with cudaGetSymbolAddress (with that
-// device current) and passed to the kernels like any workspace.
+// device current) and passed to the kernels like any workspace. The cached
+// address is tied to the CUDA context that was current when it was fetched:
+// a host that makes its own driver context on the device, or that reset the
+// device (which destroys the primary context), gets the address looked up
+// again in its own context.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -36,20 +42,44 @@ static __device__ __align__(256) unsigned char
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of this device's scratch array; set up on the first call
-// per device (the device is current here).
+// The driver's cuCtxGetCurrent, reached through the runtime (no link
+// dependency on libcuda); null if the driver does not provide it.
+PFN_cuCtxGetCurrent_v4000 ctx_get_current_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(ptr);
+    }
+  });
+  return fn;
+}
+
+// Device address of this device's scratch array in the current context; set
+// up on the first call per device and context (the device is current here).
 cudaError_t scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  CUcontext ctx = nullptr;
+  PFN_cuCtxGetCurrent_v4000 get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS) return cudaErrorUnknown;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (g_scratch_ptr[dev] == nullptr || ctx == nullptr || g_scratch_ctx[dev] != ctx) {
     void* ptr = nullptr;
+    // binds the device's primary context first if no context is current yet
     e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
     if (e != cudaSuccess) return e;
+    if (ctx == nullptr && get_ctx(&ctx) != CUDA_SUCCESS) return cudaErrorUnknown;
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;

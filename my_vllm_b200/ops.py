@@ -251,10 +251,18 @@ def build_slot_mapping(
     block_size: int,
     num_tokens: int,
     out: torch.Tensor | None = None,
+    *,
+    num_blocks: int | None = None,
+    max_blocks: int | None = None,
+    status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Cache slots of the new tokens, computed on the GPU from the batch
     metadata (the host loop of ModelRunner.prepare_model_input,
-    nanovllm/engine/model_runner.py:414-425). Returns int32 [num_tokens]."""
+    nanovllm/engine/model_runner.py:414-425). Returns int32 [num_tokens].
+
+    Positions past a row's ``max_blocks`` columns (default: the table width)
+    or page ids >= ``num_blocks`` (default: no pool bound) give slot -1 and set
+    ``STATUS_SLOT_OUT_OF_RANGE`` in ``status``."""
     for name, t in (("block_tables", block_tables), ("seq_lens", seq_lens),
                     ("query_start_loc", query_start_loc)):
         _require_cuda(name, t)
@@ -265,17 +273,101 @@ def build_slot_mapping(
     num_seqs = seq_lens.numel()
     if query_start_loc.numel() != num_seqs + 1 or block_tables.size(0) != num_seqs:
         raise ValueError("metadata lengths do not match num_seqs")
+    width = block_tables.size(1) if max_blocks is None else int(max_blocks)
+    if not 0 <= width <= block_tables.size(1):
+        raise ValueError("max_blocks must lie within the table width")
+    pool = (1 << 62) if num_blocks is None else int(num_blocks)
     if out is None:
         out = torch.empty(num_tokens, dtype=torch.int32, device=seq_lens.device)
     elif out.dtype != torch.int32 or out.numel() != num_tokens or not out.is_contiguous():
         raise ValueError("out must be a contiguous int32 tensor of num_tokens entries")
     rc = _native.load_library().b200_build_slot_mapping(
-        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(),
-        query_start_loc.data_ptr(), num_seqs, int(num_tokens), int(block_size),
-        out.data_ptr(), _stream_handle(seq_lens.device),
+        block_tables.data_ptr(), max(block_tables.stride(0), width), width, pool,
+        seq_lens.data_ptr(), query_start_loc.data_ptr(), num_seqs, int(num_tokens),
+        int(block_size), out.data_ptr(), _ptr(status), _stream_handle(seq_lens.device),
     )
     _native.check(rc, "b200_build_slot_mapping")
     return out
+
+
+def build_block_tables_packed(
+    packed: torch.Tensor,
+    num_seqs: int,
+    max_blocks: int,
+    out: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Padded ``[num_seqs, max_blocks]`` int32 block tables (-1 past each
+    list) from one packed device buffer: ``packed[: num_seqs + 1]`` are the
+    list offsets and ``packed[num_seqs + 1:]`` the block ids back to back
+    (ModelRunner.prepare_block_tables, nanovllm/engine/model_runner.py:354-358,
+    without the host padding)."""
+    _require_cuda("packed", packed)
+    if packed.dtype != torch.int32 or packed.dim() != 1 or not packed.is_contiguous():
+        raise TypeError("packed must be a contiguous 1-D int32 tensor")
+    if packed.numel() < num_seqs + 1:
+        raise ValueError("packed holds fewer than num_seqs + 1 offsets")
+    if out is None:
+        out = torch.empty(num_seqs, max_blocks, dtype=torch.int32, device=packed.device)
+    elif (out.dtype != torch.int32 or out.dim() != 2 or out.size(0) != num_seqs
+          or out.size(1) < max_blocks or out.stride(1) != 1):
+        raise ValueError("out must be int32 [num_seqs, >= max_blocks] with contiguous rows")
+    rc = _native.load_library().b200_build_block_tables(
+        packed.data_ptr() + 4 * (num_seqs + 1), packed.data_ptr(), int(num_seqs),
+        int(max_blocks), out.data_ptr(), out.stride(0) if num_seqs else max_blocks,
+        _ptr(status), _stream_handle(packed.device),
+    )
+    _native.check(rc, "b200_build_block_tables")
+    return out
+
+
+class BlockTableBuilder:
+    """Per-step block tables built on the GPU with ONE host-to-device copy.
+
+    ``build(block_lists)`` takes the scheduled sequences' ``block_table``
+    lists, packs their offsets and ids into a pinned host buffer, copies it
+    with one ``cudaMemcpyAsync`` to a device staging buffer and lets
+    ``b200_build_block_tables`` write the -1-padded table. Both buffers are
+    owned by the builder and grow on demand; the pinned buffer is reused only
+    after the previous step's copy has completed (an event guards it)."""
+
+    def __init__(self, device: torch.device | str):
+        self.device = torch.device(device)
+        self._host: torch.Tensor | None = None
+        self._dev: torch.Tensor | None = None
+        self._copied: torch.cuda.Event | None = None
+
+    def _buffers(self, n: int):
+        if self._host is None or self._host.numel() < n:
+            size = max(n, 2 * (self._host.numel() if self._host is not None else 0), 4096)
+            self._host = torch.empty(size, dtype=torch.int32, pin_memory=True)
+            self._dev = torch.empty(size, dtype=torch.int32, device=self.device)
+            self._copied = None
+        elif self._copied is not None:
+            self._copied.synchronize()
+        return self._host, self._dev
+
+    def build(self, block_lists, out: torch.Tensor | None = None,
+              status: torch.Tensor | None = None) -> torch.Tensor:
+        num_seqs = len(block_lists)
+        counts = [len(b) for b in block_lists]
+        max_blocks = max(counts, default=0)
+        total = sum(counts)
+        host, dev = self._buffers(num_seqs + 1 + total)
+        view = host.numpy()
+        view[0] = 0
+        if num_seqs:
+            import numpy as np
+
+            np.cumsum(counts, out=view[1: num_seqs + 1])
+            flat = [i for b in block_lists for i in b]
+            view[num_seqs + 1: num_seqs + 1 + total] = flat
+        n = num_seqs + 1 + total
+        dev[:n].copy_(host[:n], non_blocking=True)
+        if self._copied is None:
+            self._copied = torch.cuda.Event()
+        self._copied.record(torch.cuda.current_stream(self.device))
+        return build_block_tables_packed(dev[:n], num_seqs, max_blocks, out=out, status=status)
 
 
 def paged_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor,

@@ -14,6 +14,6 @@ from .paged_attention import (  # noqa: F401
     paged_attention_from_tables,
     to_f32,
 )
-from .metadata import slot_mapping  # noqa: F401,E402
+from .metadata import block_tables, slot_mapping  # noqa: F401,E402
 from .rope import cos_sin_cache, rms_norm, rope_neox  # noqa: F401,E402
 from . import fp8  # noqa: F401,E402

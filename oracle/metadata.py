@@ -31,3 +31,10 @@ def slot_mapping(block_tables, num_cached_tokens, num_context_tokens, block_size
                 end = (table[i] + 1) * block_size
             slots.extend(range(start, end))
     return slots
+
+
+def block_tables(block_lists):
+    """ModelRunner.prepare_block_tables (nanovllm/engine/model_runner.py:354-358):
+    every sequence's block list padded with -1 to the longest one."""
+    width = max(len(b) for b in block_lists)
+    return [list(b) + [-1] * (width - len(b)) for b in block_lists]

@@ -16,9 +16,33 @@ GOLDEN = REPO / "tests" / "golden"
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
+# The engine this backend plugs into (nanovllm), installed unmodified into
+# baseline/_ref by baseline/install_ref.py, plus its copied test helpers.
+from baseline import install_ref  # noqa: E402
+
+ENGINE_INSTALLED = install_ref.add_to_path()
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+def pytest_report_header(config):
+    if not ENGINE_INSTALLED:
+        return "engine: nanovllm NOT installed in baseline/_ref (engine tests skip)"
+    import nanovllm
+
+    return f"engine: nanovllm from {Path(nanovllm.__file__).parent} (ENGINE_CONTRACT=True)"
+
+
+@pytest.fixture(scope="session")
+def engine():
+    """The installed reference engine; skips the test where it is absent."""
+    if not ENGINE_INSTALLED:
+        pytest.skip("reference engine not installed (python baseline/install_ref.py <source>)")
+    import nanovllm
+
+    return nanovllm
 
 
 def load_golden(name: str) -> dict:

@@ -21,6 +21,7 @@ uint16 bit patterns.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import sys
 from pathlib import Path
@@ -150,7 +151,7 @@ def attention_case(reference_fn, name):
 def config1_inputs():
     """Config 1 (the CPU parity configuration) with unused pool blocks zeroed."""
     sys.path.insert(0, str(REPO))
-    from my_vllm_b200 import workloads
+    import workloads
 
     w = workloads.config1(device="cpu")
     used = torch.zeros(w.k_cache.size(0), dtype=torch.bool)
@@ -231,8 +232,11 @@ def rope_case():
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("NANOVLLM_REFERENCE"),
+                    help="reference source tree (default: $NANOVLLM_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set NANOVLLM_REFERENCE")
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "tests"))

@@ -46,6 +46,17 @@ def sample_oracle(w, seq_ids, k_cache=None, v_cache=None):
     return out, q_rows
 
 
+def oracle_all_rows(w, chunk_seqs: int = 32, k_cache=None, v_cache=None) -> np.ndarray:
+    """fp32 oracle output for EVERY row of the workload [T, Hq, D], computed
+    in chunks of sequences so the host holds one chunk's pages at a time."""
+    expected = np.empty((w.num_tokens, w.num_q_heads, w.head_dim), dtype=np.float32)
+    for start in range(0, w.num_seqs, chunk_seqs):
+        ids = list(range(start, min(start + chunk_seqs, w.num_seqs)))
+        out, rows = sample_oracle(w, ids, k_cache, v_cache)
+        expected[rows] = out
+    return expected
+
+
 def sample_oracle_fp8(w, seq_ids, k8, v8, k_scale, v_scale):
     """fp32 oracle over FP8 caches: the sampled sequences' pages dequantised
     (stored x scale), q in fp32; returns (output [rows, Hq, D], rows)."""

@@ -7,9 +7,10 @@ import pytest
 import torch
 
 from conftest import from_storage, golden_module, load_golden
-from my_vllm_b200 import B200PagedBackend, ops, workloads
+from my_vllm_b200 import B200PagedBackend, ops
+import workloads
 from my_vllm_b200.contract import AttentionRoute, BatchType, CommonAttentionMetadata
-from parity import MAX_ABS, assert_close_to_oracle, sample_oracle
+from parity import MAX_ABS, assert_close_to_oracle, oracle_all_rows, sample_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -102,8 +103,8 @@ def test_config2_decode_full_size(cuda_device):
     backend = _backend(w)
     out, plan = _append_and_run(w, backend, cuda_device)
     assert plan.route is AttentionRoute.DECODE
-    expected, rows = sample_oracle(w, [0, 1, 77, 128, 200, 255])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    # every one of the 256 rows against the oracle
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
 
     # Paging property at full size: the same logical cache laid out over a
     # different permutation of physical blocks gives bit-identical output.
@@ -125,13 +126,14 @@ def test_config2_decode_full_size(cuda_device):
 
 
 def test_config2_padded_batch_rows(cuda_device):
-    """264 appended rows, 8 of them CUDA-graph padding (slot -1): attention
-    over the 256 real rows is unchanged by the padding."""
-    w = workloads.config2(device=cuda_device, padded=True, batch=64, ctx=1024)
+    """Config 2 at full size (B 256, ctx 4096) with 264 appended rows, 8 of them
+    CUDA-graph padding (slot -1): every real row matches the oracle over the
+    cache as the append left it."""
+    w = workloads.config2(device=cuda_device, padded=True)
+    assert w.key.size(0) == 264 and w.num_tokens == 256
     backend = _backend(w)
     out, _ = _append_and_run(w, backend, cuda_device)
-    expected, rows = sample_oracle(w, [0, 31, 63])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
 
 
 @pytest.mark.parametrize("parts", [1, 3, 7])
@@ -149,20 +151,20 @@ def test_config3_mixed_chunked_prefill(cuda_device):
     backend = _backend(w)
     out, plan = _append_and_run(w, backend, cuda_device)
     assert plan.route is AttentionRoute.MIXED_SPLIT and plan.batch_type is BatchType.MIXED
-    # every prefill row (4 x 512 tokens over shared prefixes) and a decode sample
-    expected, rows = sample_oracle(w, [0, 1, 2, 3])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
-    expected, rows = sample_oracle(w, [4, 50, 127])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    # all 2172 rows: 4 x 512 prefill tokens over shared prefixes + 124 decode rows
+    assert out.size(0) == 2172
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
 
 
-def test_config4_tensor_parallel_shard(cuda_device):
-    """One rank's shard of Qwen3-32B heads at tp 8 (8 q heads on 1 KV head)."""
-    w = workloads.config4(device=cuda_device, tp=8, batch=128)
+@pytest.mark.parametrize("tp", [8, 2])
+def test_config4_tensor_parallel_shard(cuda_device, tp):
+    """One rank's shard of Qwen3-32B heads (64 q / 8 kv) at tp 8 (8 q heads on
+    1 KV head) and tp 2 (32 on 4), one layer of the full B 512 batch with
+    context U[1024, 8192]: every row against the oracle."""
+    w = workloads.config4(device=cuda_device, tp=tp, batch=512)
     backend = _backend(w)
     out, _ = _append_and_run(w, backend, cuda_device)
-    expected, rows = sample_oracle(w, [0, 64, 127])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
 
 
 @pytest.mark.parametrize("block_size", [16, 256])
@@ -171,8 +173,7 @@ def test_config5_long_context_split_kv(cuda_device, block_size):
     backend = _backend(w)
     out, plan = _append_and_run(w, backend, cuda_device)
     assert plan.metadata.decode_plan.num_parts > 1
-    expected, rows = sample_oracle(w, [0, 31])
-    assert_close_to_oracle(out[rows], expected, w.q.dtype)
+    assert_close_to_oracle(out, oracle_all_rows(w, chunk_seqs=8), w.q.dtype)
 
 
 def test_fp16_decode_tolerance(cuda_device):
@@ -351,3 +352,45 @@ def test_prefill_q_view_of_fused_qkv(cuda_device, hq, hkv):
     assert torch.equal(outs[0], outs[1])
     expected, rows = sample_oracle(w, list(range(len(q_lens))))
     assert_close_to_oracle(outs[1][rows], expected, w.q.dtype)
+
+
+@pytest.mark.parametrize("kv_fp8", [False, True])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (64, 8)])
+def test_prefill_output_into_a_padded_view(cuda_device, hq, hkv, kv_fp8):
+    """``out`` as a view into a wider NaN-filled buffer (token stride larger
+    than Hq x D): whole output tiles leave by TMA store through a tensor map
+    with that stride, partial tiles by row stores. GQA groups 4 and 8 with
+    chunk lengths that are not multiples of 128 / group mix both kinds in one
+    CTA. The padding columns must stay NaN and the rows must equal the
+    contiguous-output result bit for bit and the oracle within tolerance."""
+    from parity import sample_oracle_fp8
+
+    q_lens = [300, 77, 129, 513]
+    kv_lens = [300, 1000, 129, 2000]
+    w = workloads.small_case(q_lens, kv_lens, len(q_lens), Hq=hq, Hkv=hkv, device=cuda_device)
+    kc, vc, scales = w.k_cache, w.v_cache, {}
+    if kv_fp8:
+        ks, vs = 0.03, 0.02
+        kc, vc = workloads.to_fp8_cache(w.k_cache, ks), workloads.to_fp8_cache(w.v_cache, vs)
+        scales = dict(k_scale=torch.tensor([ks], dtype=torch.float32, device=cuda_device),
+                      v_scale=torch.tensor([vs], dtype=torch.float32, device=cuda_device))
+    T, D = w.q.size(0), w.head_dim
+    pad = 3 * D
+    wide = torch.full((T, hq * D + pad), float("nan"), dtype=w.q.dtype, device=cuda_device)
+    out_view = wide[:, : hq * D].view(T, hq, D)
+    assert out_view.stride(0) == hq * D + pad
+    out_flat = torch.full_like(w.q, float("nan"))
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for out in (out_view, out_flat):
+        ops.paged_prefill(w.q, kc, vc, w.block_tables, w.seq_lens, w.query_start_loc, out,
+                          max(q_lens), D ** -0.5, status=status, **scales)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.isnan(wide[:, hq * D:].float()).all(), "padding columns were written"
+    assert torch.equal(out_view.view(torch.int16), out_flat.view(torch.int16))
+    ids = list(range(len(q_lens)))
+    if kv_fp8:
+        expected, rows = sample_oracle_fp8(w, ids, kc, vc, 0.03, 0.02)
+    else:
+        expected, rows = sample_oracle(w, ids)
+    assert_close_to_oracle(out_view[rows], expected, w.q.dtype)

@@ -8,6 +8,8 @@ from unittest.mock import patch
 import pytest
 import torch
 
+pytest.importorskip("nanovllm", reason="reference engine not installed in baseline/_ref")
+
 from my_vllm_b200 import B200PagedBackend, B200PagedMetadata, ops
 from my_vllm_b200.backend import classify_batch, validate_common_metadata
 from my_vllm_b200.contract import (

@@ -9,7 +9,8 @@ import torch
 
 import oracle
 from conftest import storage
-from my_vllm_b200 import _native, ops, workloads
+from my_vllm_b200 import _native, ops
+import workloads
 from parity import MAX_ABS, assert_close_to_oracle, sample_oracle_fp8
 
 pytestmark = pytest.mark.gpu

@@ -7,7 +7,8 @@ import torch
 
 import oracle
 from conftest import from_storage, load_golden, storage
-from my_vllm_b200 import _native, ops, workloads
+from my_vllm_b200 import _native, ops
+import workloads
 from parity import append_reference_rows
 
 pytestmark = pytest.mark.gpu
@@ -154,3 +155,74 @@ def test_device_slot_mapping_matches_oracle_on_config3(cuda_device):
                                  w.num_tokens)
     assert got.tolist() == expected
     assert expected == w.extra["slots_host"][: w.num_tokens]
+
+
+def test_device_slot_mapping_bounds_checked(cuda_device):
+    """A row shorter than its sequence needs, or a page id outside the pool,
+    gives slot -1 and the out-of-range status bit instead of a read past the
+    table row."""
+    dev = cuda_device
+    # the table has 2 columns; sequence 1 needs 3 blocks for 40 tokens
+    bt = torch.tensor([[7, 4], [9, 3]], dtype=torch.int32, device=dev)
+    lens = torch.tensor([19, 40], dtype=torch.int32, device=dev)
+    qsl = torch.tensor([0, 3, 5], dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    slots = ops.build_slot_mapping(bt, lens, qsl, 16, 5, status=status, num_blocks=16)
+    assert slots.tolist() == [64, 65, 66, -1, -1]
+    assert int(status.item()) == _native.STATUS_SLOT_OUT_OF_RANGE
+    # a page id beyond the pool (page 9, num_blocks 8)
+    lens = torch.tensor([19, 5], dtype=torch.int32, device=dev)
+    status.zero_()
+    slots = ops.build_slot_mapping(bt, lens, qsl, 16, 5, status=status, num_blocks=8)
+    assert slots.tolist() == [64, 65, 66, -1, -1]
+    assert int(status.item()) == _native.STATUS_SLOT_OUT_OF_RANGE
+    # in range: no report
+    status.zero_()
+    slots = ops.build_slot_mapping(bt, lens, qsl, 16, 5, status=status, num_blocks=16)
+    assert slots.tolist() == [64, 65, 66, 147, 148]
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+
+
+def test_device_block_tables_known_answer(cuda_device):
+    # ModelRunner.prepare_block_tables on the reference's metadata test
+    # (tests/test_model_runner_metadata.py:138-187): [[7, 4], [9]] -> [[7, 4], [9, -1]]
+    builder = ops.BlockTableBuilder(cuda_device)
+    got = builder.build([[7, 4], [9]])
+    assert got.tolist() == [[7, 4], [9, -1]]
+    assert got.dtype == torch.int32 and got.device.type == "cuda"
+    got = builder.build([[2], [4, 5]])
+    assert got.tolist() == oracle.block_tables([[2], [4, 5]])
+
+
+def test_device_block_tables_match_oracle_on_config3_and_config4(cuda_device):
+    builder = ops.BlockTableBuilder(cuda_device)
+    for w in (workloads.config3(device=cuda_device),
+              workloads.config4(device=cuda_device, tp=8, batch=512)):
+        lists = [row[: c].tolist() for row, c in zip(w.block_tables.cpu(), w.block_counts)]
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        got = builder.build(lists, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert got.tolist() == oracle.block_tables(lists)
+        # identical to the workload's own host-padded table
+        assert torch.equal(got, w.block_tables)
+
+
+def test_device_block_tables_into_a_wider_buffer_and_cut_rows(cuda_device):
+    """Rows land in a caller buffer wider than the longest list (the
+    full-decode graph's fixed-width table); columns past max_blocks are left
+    alone, and a list longer than the requested width is cut and reported."""
+    dev = cuda_device
+    lists = [[5, 6, 7], [1], []]
+    packed = torch.tensor([0, 3, 4, 4, 5, 6, 7, 1], dtype=torch.int32, device=dev)
+    out = torch.full((3, 6), 99, dtype=torch.int32, device=dev)
+    ops.build_block_tables_packed(packed, 3, 3, out=out)
+    assert out.tolist() == [[5, 6, 7, 99, 99, 99], [1, -1, -1, 99, 99, 99],
+                            [-1, -1, -1, 99, 99, 99]]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    cut = ops.build_block_tables_packed(packed, 3, 2, status=status)
+    torch.cuda.synchronize()
+    assert cut.tolist() == [[5, 6], [1, -1], [-1, -1]]
+    assert int(status.item()) == _native.STATUS_PAGE_OUT_OF_RANGE
+    del lists

@@ -33,7 +33,8 @@ def _init(rank, world, port, timeout_s=60):
 def _sharded_worker(rank, world, port, result_path):
     sys.path.insert(0, str(REPO))
     import oracle
-    from my_vllm_b200 import sharding, workloads
+    import workloads
+    from my_vllm_b200 import sharding
 
     _init(rank, world, port)
     w = workloads.config1(device="cpu")
@@ -60,7 +61,7 @@ def _sharded_worker(rank, world, port, result_path):
 def test_kv_head_sharding_matches_unsharded(tmp_path):
     sys.path.insert(0, str(REPO))
     import oracle
-    from my_vllm_b200 import workloads
+    import workloads
 
     result = tmp_path / "sharded.npy"
     mp.start_processes(_sharded_worker, args=(2, _free_port(), str(result)), nprocs=2,

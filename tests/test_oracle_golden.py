@@ -101,6 +101,13 @@ def test_slot_mapping_known_answers():
     assert oracle.slot_mapping([[], []], [0, 0], [4, 2], 16) == [-1] * 6
 
 
+def test_block_tables_known_answer():
+    # tests/test_model_runner_metadata.py:181-184: [[7, 4], [9]] pads to [[7, 4], [9, -1]]
+    assert oracle.block_tables([[7, 4], [9]]) == [[7, 4], [9, -1]]
+    assert oracle.block_tables([[2], [4, 5]]) == [[2, -1], [4, 5]]
+    assert oracle.block_tables([[1, 2, 3]]) == [[1, 2, 3]]
+
+
 def test_rope_and_rmsnorm_match_reference():
     mg = golden_module()
     g = load_golden("rope")

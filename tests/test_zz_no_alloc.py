@@ -13,8 +13,9 @@ import ctypes
 import pytest
 import torch
 
-from my_vllm_b200 import _native, ops, workloads
-from parity import MAX_ABS
+from my_vllm_b200 import _native, ops
+import workloads
+from parity import MAX_ABS, assert_close_to_oracle, oracle_all_rows
 
 pytestmark = pytest.mark.gpu
 
@@ -53,6 +54,38 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls(cuda_device):
         assert torch.isfinite(out.float()).all()
         err = (out.float() - expected.float()).abs().max().item()
         assert err <= MAX_ABS[torch.bfloat16], err
+
+
+def test_noalloc_ragged_batch_after_a_larger_call_matches_the_oracle(cuda_device):
+    """The scratch keeps the previous call's partials. A ragged batch whose
+    short sequences leave most partitions empty, run right after a larger
+    call that filled every partition, must still merge only its own
+    partitions: checked on every row against the fp32 oracle and against the
+    workspace entry point."""
+    scale = 128 ** -0.5
+    big = workloads.config2(device=cuda_device, batch=32, ctx=4000, pool_blocks=8192)
+    plan_big = ops.plan_decode(32, big.num_q_heads, big.num_kv_heads, big.head_dim,
+                               big.block_size, 4000, force_num_parts=8)
+    out_big = torch.empty_like(big.q)
+    rc = _noalloc_decode(big.q, big.k_cache, big.v_cache, big.block_tables, big.seq_lens,
+                         out_big, plan_big, scale)
+    assert rc == _native.B200_OK, _native.load_library().b200_last_error()
+    lens = [1, 17, 300, 4000, 2, 1029, 16, 3999, 5, 640]
+    w = workloads.small_case([1] * len(lens), lens, 0, Hq=32, Hkv=8, device=cuda_device)
+    plan = ops.plan_decode(len(lens), 32, 8, 128, 16, max(lens), force_num_parts=8,
+                           total_kv_tokens=sum(lens))
+    assert plan.num_parts == 8
+    out = torch.full_like(w.q, float("nan"))
+    rc = _noalloc_decode(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, out, plan,
+                         scale)
+    assert rc == _native.B200_OK, _native.load_library().b200_last_error()
+    workspace = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=cuda_device)
+    expected = torch.empty_like(w.q)
+    ops.paged_decode(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, expected, plan,
+                     scale, workspace)
+    torch.cuda.synchronize()
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
+    assert (out.float() - expected.float()).abs().max().item() <= MAX_ABS[torch.bfloat16]
 
 
 def test_noalloc_decode_rejects_batches_beyond_its_scratch(cuda_device):

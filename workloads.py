@@ -19,7 +19,6 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .contract import CommonAttentionMetadata
 
 SEED_BASE = 2026
 
@@ -52,8 +51,10 @@ class Workload:
     def num_tokens(self) -> int:
         return self.q.size(0)
 
-    def common_metadata(self) -> CommonAttentionMetadata:
+    def common_metadata(self):
         """The engine's per-step metadata for this batch (trusted, host ints)."""
+        from my_vllm_b200.contract import CommonAttentionMetadata
+
         qsl = self.query_start_loc.tolist() if self.query_start_loc.device.type == "cpu" else (
             self.extra["qsl_host"]
         )
@@ -285,6 +286,8 @@ class LayeredDecode:
         return self.kv_cache[0, i], self.kv_cache[1, i]
 
     def common_metadata(self):
+        from my_vllm_b200.contract import CommonAttentionMetadata
+
         B = len(self.seq_lens_host)
         return CommonAttentionMetadata(
             num_prefill_seqs=0, num_decode_seqs=B, num_prefill_tokens=0, num_decode_tokens=B,
