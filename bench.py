@@ -40,6 +40,13 @@ from pathlib import Path
 import torch
 
 REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+from baseline import install_ref  # noqa: E402
+
+# The engine this backend plugs into (nanovllm), installed unmodified into
+# baseline/_ref, and the reference's test helpers the reference arm times.
+ENGINE_INSTALLED = install_ref.add_to_path()
 METRIC = "paged decode attn+KV-append HBM GB/s and tokens/s at 1/2/4/8 B200"
 TOTAL_Q_HEADS, TOTAL_KV_HEADS, HEAD_DIM, BLOCK_SIZE = 32, 8, 128, 16
 BATCH, CONTEXT = 256, 4096
