@@ -261,6 +261,12 @@ B200_API int b200_paged_decode_plan(int32_t num_seqs, int32_t num_q_heads,
  *      block_table_stride; seq_lens: int32 [num_seqs], each >= 1 and
  *      including the token being decoded (model_runner.py:404-406).
  * workspace: plan->workspace_bytes of device memory (may be NULL when 0).
+ * The kernel is launched as a programmatic dependent of the kernel before it
+ * on `stream`: it may start while that kernel runs, and it holds its cache
+ * reads until that kernel has completed. q, the metadata and the workspace
+ * must therefore be written before the previous kernel STARTS (an earlier
+ * launch or copy); the cache may be written by the previous kernel itself
+ * (the KV append of the same step, b200_store_kvcache).
  * Replaces BatchDecodeWithPagedKVCacheWrapper.run as called from
  * FlashInferBackend.forward (attention_backend.py:995-997, 1020-1025).
  */

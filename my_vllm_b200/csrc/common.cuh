@@ -55,6 +55,18 @@ __device__ __forceinline__ void report_status(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
+// ------------------------------------------ programmatic dependent launch --
+// A kernel launched with programmatic stream serialization may start while
+// the kernel before it on the stream is still running; it must execute
+// pdl_wait() before touching anything that kernel writes (pdl_wait returns
+// once that grid has completed and its writes are visible). The earlier
+// kernel calls pdl_launch_dependents() to let the dependent grid start.
+// Both are no-ops for kernels launched the ordinary way.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count)

@@ -45,6 +45,9 @@ __global__ void __launch_bounds__(256)
                      int64_t vecs_per_row, int64_t num_slots,
                      int32_t* status) {
   using V = typename VecType<kVec>::type;
+  // the decode that follows may start its prologue now; it waits for this
+  // grid to complete before it reads the cache
+  pdl_launch_dependents();
   // Work item = (token, tensor in {K, V}, vector within row).
   const int64_t per_token = 2 * vecs_per_row;
   const int64_t total = num_tokens * per_token;
@@ -161,6 +164,7 @@ __global__ void __launch_bounds__(256)
                          int64_t cache_slot_stride, const int32_t* __restrict__ slot_mapping,
                          int64_t num_tokens, int64_t vecs_per_row, const float* k_scale,
                          const float* v_scale, int64_t num_slots, int32_t* status) {
+  pdl_launch_dependents();
   // reciprocals of the dequantisation scales, correctly rounded to fp32
   const float ks = __frcp_rn(k_scale != nullptr ? __ldg(k_scale) : 1.f);
   const float vs = __frcp_rn(v_scale != nullptr ? __ldg(v_scale) : 1.f);

@@ -201,6 +201,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? (kWideGroup ? 3 : 4)
     }
   };
 
+  // Everything above reads only metadata and q. The cache may still be
+  // receiving this step's rows from the append kernel launched just before
+  // (this kernel is launched as its programmatic dependent): wait for it.
+  pdl_wait();
   const int prologue = my_tiles < kStages ? my_tiles : kStages;
   if (lane == 0)
     for (int j = 0; j < prologue; ++j) issue(j);
@@ -490,9 +494,20 @@ static cudaError_t launch_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   constexpr int kSmem = decode_smem_bytes(kFp8);
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kSmem);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.num_parts, num_kv_heads, num_seqs);
-  kernel<<<grid, kDecodeWarps * 32, kSmem, stream>>>(mk, mv, p);
-  e = cudaGetLastError();
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream (the KV append of the same step): the CTAs' prologue overlaps the
+  // append, and pdl_wait() holds the cache reads until it has completed.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.num_parts, num_kv_heads, num_seqs);
+  cfg.blockDim = dim3(kDecodeWarps * 32);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, mk, mv, p);
   if (e != cudaSuccess) return e;
   if (p.num_parts > 1) {
     decode_reduce_kernel<T><<<dim3(p.num_q_heads, num_seqs), kHeadDim, 0, stream>>>(p);
