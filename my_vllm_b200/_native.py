@@ -177,6 +177,31 @@ def load_library() -> ctypes.CDLL:
         return lib
 
 
+TORCH_OPS_PATH = LIBRARY_PATH.with_name("libb200_torch_ops.so")
+_torch_ops_loaded = False
+
+
+def load_torch_ops():
+    """Register the ``torch.ops.b200`` operators (kv_append, paged_decode,
+    paged_prefill) from the in-tree operator library; returns ``torch.ops.b200``.
+    RuntimeError if either library is missing."""
+    global _torch_ops_loaded
+    import torch
+
+    if not _torch_ops_loaded:
+        with _lock:
+            if not _torch_ops_loaded:
+                if not TORCH_OPS_PATH.exists():
+                    raise RuntimeError(
+                        f"B200 torch operator library not built: {TORCH_OPS_PATH} is missing "
+                        "(run `python -m my_vllm_b200.build`)"
+                    )
+                torch.ops.load_library(str(TORCH_OPS_PATH))
+                _torch_ops_loaded = True
+    load_library()
+    return torch.ops.b200
+
+
 def library_available() -> bool:
     try:
         load_library()

@@ -18,6 +18,11 @@ CSRC_DIR = PACKAGE_DIR / "csrc"
 INCLUDE_DIR = PACKAGE_DIR.parent / "include"
 LIBRARY_NAME = "libb200_paged_attn.so"
 LIBRARY_PATH = PACKAGE_DIR / LIBRARY_NAME
+# The torch.ops.b200.* operators: a C++ layer over the C ABI, linked against
+# the kernel library (found beside it through its SONAME and an $ORIGIN rpath).
+TORCH_OPS_NAME = "libb200_torch_ops.so"
+TORCH_OPS_PATH = PACKAGE_DIR / TORCH_OPS_NAME
+TORCH_OPS_SOURCES = ("torch_ops.cpp",)
 
 SOURCES = (
     "kv_append.cu",
@@ -39,6 +44,8 @@ NVCC_FLAGS = (
     "-Xcompiler",
     "-fvisibility=hidden",
     "-shared",
+    "-Xlinker",
+    "-soname=" + LIBRARY_NAME,
 )
 
 
@@ -68,7 +75,49 @@ def is_stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every kernel into one shared library; returns its path."""
+    """Compile every kernel into one shared library, then the torch operator
+    library over it; returns the kernel library's path."""
+    _build_kernels(force, verbose)
+    build_torch_ops(force)
+    return LIBRARY_PATH
+
+
+def build_torch_ops(force: bool = False) -> Path:
+    """Build ``libb200_torch_ops.so`` (TORCH_LIBRARY ``b200``) with
+    torch.utils.cpp_extension, the way the reference builds its own op
+    (setup.py:7-14), into an in-tree build folder, and place it beside the
+    kernel library."""
+    sources = [CSRC_DIR / name for name in TORCH_OPS_SOURCES]
+    inputs = sources + sorted(INCLUDE_DIR.glob("*.h")) + [LIBRARY_PATH]
+    if (not force and TORCH_OPS_PATH.exists()
+            and all(p.stat().st_mtime <= TORCH_OPS_PATH.stat().st_mtime for p in inputs)):
+        return TORCH_OPS_PATH
+    import ctypes
+
+    import torch.utils.cpp_extension as cpp_extension
+
+    # cpp_extension.load() opens the result from the build folder; with the
+    # kernel library already loaded its SONAME satisfies the dependency there
+    ctypes.CDLL(str(LIBRARY_PATH), mode=ctypes.RTLD_GLOBAL)
+    build_dir = PACKAGE_DIR / "_build" / "torch_ops"
+    build_dir.mkdir(parents=True, exist_ok=True)
+    built = cpp_extension.load(
+        name="b200_torch_ops",
+        sources=[str(p) for p in sources],
+        extra_include_paths=[str(INCLUDE_DIR)],
+        extra_cflags=["-O2", "-std=c++17"],
+        extra_ldflags=[f"-L{PACKAGE_DIR}", f"-l:{LIBRARY_NAME}", "-Wl,-rpath,\\$$ORIGIN"],
+        build_directory=str(build_dir),
+        with_cuda=True,
+        is_python_module=False,
+        verbose=False,
+    )
+    del built
+    shutil.copy2(build_dir / "b200_torch_ops.so", TORCH_OPS_PATH)
+    return TORCH_OPS_PATH
+
+
+def _build_kernels(force: bool = False, verbose: bool = False) -> Path:
     if not force and not is_stale():
         return LIBRARY_PATH
     tmp = LIBRARY_PATH.with_suffix(".so.tmp")

@@ -1,8 +1,11 @@
-"""Torch-tensor front ends of the three kernels.
+"""Torch-tensor front ends of the kernels.
 
 Each function checks its tensors the way the reference checks them before
-its own kernels run, then calls the C ABI on the current CUDA stream. There
-is no CPU path: a CPU tensor or a missing library raises.
+its own kernels run (raising the reference's error types), then calls the
+kernel on the current CUDA stream: the append, decode and prefill through
+the ``torch.ops.b200`` operators (``csrc/torch_ops.cpp``, a TORCH_LIBRARY
+layer over the C ABI), the rest through the C ABI directly. There is no CPU
+path: a CPU tensor or a missing library raises.
 """
 
 from __future__ import annotations
@@ -24,6 +27,12 @@ def _stream_handle(device: torch.device) -> int:
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def _ops():
+    """``torch.ops.b200`` (kv_append, paged_decode, paged_prefill), registered
+    from the in-tree operator library on first use."""
+    return _native.load_torch_ops()
 
 
 def _require_cuda(name: str, t: torch.Tensor) -> None:
@@ -81,16 +90,9 @@ def store_kvcache(
         raise ValueError("slot_mapping must be a contiguous 1-D tensor")
     if N == 0:
         return
-    num_slots = k_cache.size(0) * k_cache.size(1) if k_cache.dim() >= 2 else k_cache.numel() // D
-    lib = _native.load_library()
-    rc = lib.b200_store_kvcache(
-        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
-        k_cache.data_ptr(), v_cache.data_ptr(), D,
-        slot_mapping.data_ptr(), 1 if slot_mapping.dtype == torch.int64 else 0,
-        N, D, key.element_size(), num_slots,
-        _ptr(status), _stream_handle(key.device),
-    )
-    _native.check(rc, "b200_store_kvcache")
+    if k_cache.dim() != 4:
+        raise ValueError("caches must be [num_blocks, block_size, num_kv_heads, head_dim]")
+    _ops().kv_append(key, value, k_cache, v_cache, slot_mapping, None, None, status)
 
 
 _KV_SCALES: dict = {}
@@ -153,13 +155,7 @@ def store_kvcache_fp8(
             raise TypeError(f"{name} must be a 1-element float32 CUDA tensor")
     if N == 0:
         return
-    rc = _native.load_library().b200_store_kvcache_fp8(
-        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), _DTYPES[key.dtype],
-        k_cache.data_ptr(), v_cache.data_ptr(), D, slot_mapping.data_ptr(), N, D,
-        _ptr(k_scale), _ptr(v_scale), k_cache.size(0) * k_cache.size(1), _ptr(status),
-        _stream_handle(key.device),
-    )
-    _native.check(rc, "b200_store_kvcache_fp8")
+    _ops().kv_append(key, value, k_cache, v_cache, slot_mapping, k_scale, v_scale, status)
 
 
 def qk_norm_rope_append(
@@ -504,20 +500,15 @@ def paged_decode(
     B = q.size(0)
     if block_tables.size(0) < B or seq_lens.numel() < B:
         raise ValueError("block_tables / seq_lens must have one row per sequence")
-    cache = paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)
-    ws_ptr, ws_bytes = None, 0
+    paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)  # cached layout checks
     if plan.workspace_bytes:
         if workspace is None or workspace.numel() * workspace.element_size() < plan.workspace_bytes:
             raise ValueError("decode workspace smaller than the plan requires")
-        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    native_plan = plan.as_native()
-    rc = _native.load_library().b200_paged_decode(
-        q.data_ptr(), q.stride(0), q.stride(1), cache,
-        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(), B,
-        q.size(1), out.data_ptr(), out.stride(0), out.stride(1), float(softmax_scale),
-        native_plan, ws_ptr, ws_bytes, _ptr(status), _stream_handle(q.device),
-    )
-    _native.check(rc, "b200_paged_decode")
+    else:
+        workspace = None
+    _ops().paged_decode(q, k_cache, v_cache, block_tables, seq_lens, out, plan.num_parts,
+                        plan.part_tokens, float(softmax_scale), workspace, k_scale, v_scale,
+                        status)
     return out
 
 
@@ -555,13 +546,7 @@ def paged_prefill(
     S = seq_lens.numel() if num_seqs is None else num_seqs
     if query_start_loc.numel() < S + 1 or block_tables.size(0) < S:
         raise ValueError("query_start_loc / block_tables too short for num_seqs")
-    cache = paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)
-    rc = _native.load_library().b200_paged_prefill(
-        q.data_ptr(), q.stride(0), q.stride(1), cache,
-        block_tables.data_ptr(), block_tables.stride(0), seq_lens.data_ptr(),
-        query_start_loc.data_ptr(), S, q.size(0), int(max_q_len), q.size(1),
-        out.data_ptr(), out.stride(0), out.stride(1), float(softmax_scale),
-        _ptr(status), _stream_handle(q.device),
-    )
-    _native.check(rc, "b200_paged_prefill")
+    paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)  # cached layout checks
+    _ops().paged_prefill(q, k_cache, v_cache, block_tables, seq_lens, query_start_loc, out,
+                         int(max_q_len), float(softmax_scale), S, k_scale, v_scale, status)
     return out
