@@ -69,7 +69,9 @@ def parse_args():
                     help="skip the config 3 / config 5 / prefill / append sub-records")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="smaller batches are for profiler captures only")
-    ap.add_argument("--workload", choices=("config2", "config3", "config4", "rope_append"),
+    ap.add_argument("--workload", choices=("config2", "config3", "config4", "rope_append",
+                                           "config5_bs16", "config5_bs256", "prefill_long",
+                                           "append_64k"),
                     default="config2",
                     help="config3: mixed chunked prefill + decode (1 GPU), reports the "
                          "prefill kernel against the tensor roofline; rope_append: the "
@@ -961,6 +963,25 @@ def subrecords(device, steps, warmup):
     return records
 
 
+def run_subrecord(args):
+    """One of the default line's sub-records on its own (1 GPU), e.g. for a
+    profiler capture of just that kernel."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    fn = {"config5_bs16": lambda: measure_config5(device, 16, args.steps, args.warmup),
+          "config5_bs256": lambda: measure_config5(device, 256, args.steps, args.warmup),
+          "prefill_long": lambda: measure_prefill_long(device, args.steps, args.warmup),
+          "append_64k": lambda: measure_append(device, args.steps, args.warmup)}[args.workload]
+    rec = fn()
+    line = {"metric": f"{args.workload} ({rec['unit']})", "value": rec["value"],
+            "unit": rec["unit"], "n_gpus": 1, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": rec["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": {"workload": rec["workload"]},
+            "roofline": rec["roofline"], "gpu_launches": rec["gpu_launches"]}
+    print(json.dumps(line), flush=True)
+
+
 def run_config3(args):
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -1322,6 +1343,9 @@ def main():
         return
     if args.workload == "rope_append":
         run_rope_append(args)
+        return
+    if args.workload in ("config5_bs16", "config5_bs256", "prefill_long", "append_64k"):
+        run_subrecord(args)
         return
     if args.workload == "config4":
         if args.gpus > 1 and "WORLD_SIZE" not in os.environ:

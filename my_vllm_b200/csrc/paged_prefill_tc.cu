@@ -142,14 +142,11 @@ __device__ __forceinline__ int tc_hist_slot(int key) { return key + (key >> 6) *
 constexpr int kTcScratchInts = kTcHistInts + 4 + kTcCachedPairs;
 static_assert(kTcScratchInts * 4 <= kTcTiles * 2 * kTcHalf, "scratch lives in the Q tiles");
 
-// (sequence, row block, KV head) of grid position `pos`; `scratch` holds
-// kTcScratchInts ints of 16-byte aligned shared memory. Call with all
-// threads of the CTA. One round of metadata loads, then shared memory and
-// shuffles only: the whole CTA waits on this before any load is issued.
-__device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, int* scratch,
-                                               int& s, int& rb, int& kvh) {
+// Histogram of the (sequence, row block) pair costs, plus a cache of the
+// first kTcCachedPairs costs, in `scratch` (kTcScratchInts ints of 16-byte
+// aligned shared memory). Call with all threads of the CTA.
+__device__ __forceinline__ void tc_build_hist(const PrefillParams& p, int* scratch) {
   int* hist = scratch;                        // [kTcHistInts], key k at tc_hist_slot(k)
-  int* result = scratch + kTcHistInts;        // [2]
   int* cost = scratch + kTcHistInts + 4;      // [kTcCachedPairs]
   const int pairs = p.num_seqs * p.blocks_per_seq;
   for (int i = threadIdx.x; i < kTcHistInts / 4; i += blockDim.x)
@@ -161,71 +158,92 @@ __device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, 
     atomicAdd(&hist[tc_hist_slot(c)], 1);
   }
   __syncthreads();
+}
+
+// The pair (sequence * blocks_per_seq + row block) at position `pair_pos` of
+// the longest-first order (ties in id order), from the histogram that
+// tc_build_hist left in `scratch`. Warp-collective; the result is the same
+// in every lane.
+__device__ __forceinline__ int tc_pair_at(const PrefillParams& p, const int* scratch,
+                                          int pair_pos, int lane) {
+  const int* hist = scratch;
+  const int* cost = scratch + kTcHistInts + 4;
+  const int pairs = p.num_seqs * p.blocks_per_seq;
+  const unsigned full = 0xffffffffu;
+  // Keys in descending order: lane l owns the chunk of keys
+  // [2048 - 64(l+1), 2048 - 64l), so lower lanes hold larger costs.
+  constexpr int kPerLane = kTcCostKeys / 32;
+  const int chunk_lo = kTcCostKeys - kPerLane * (lane + 1);
+  int chunk = 0;
+#pragma unroll
+  for (int k = 0; k < kPerLane / 4; ++k) {
+    const int4 h = reinterpret_cast<const int4*>(hist + tc_hist_slot(chunk_lo))[k];
+    chunk += (h.x + h.y) + (h.z + h.w);
+  }
+  // pairs in the chunks of lower lanes (larger keys): exclusive prefix sum
+  int incl = chunk;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(full, incl, d);
+    if (lane >= d) incl += v;
+  }
+  const unsigned own = __ballot_sync(full, pair_pos >= incl - chunk && pair_pos < incl);
+  const int o = own ? __ffs(own) - 1 : 0;
+  const int before_o = __shfl_sync(full, incl - chunk, o);
+  // inside chunk o, lane l takes keys hi = top - 2l and hi - 1 (descending)
+  const int hi = kTcCostKeys - 1 - kPerLane * o - 2 * lane;
+  const int h0 = hist[tc_hist_slot(hi)], h1 = hist[tc_hist_slot(hi - 1)];
+  int incl2 = h0 + h1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(full, incl2, d);
+    if (lane >= d) incl2 += v;
+  }
+  const int first = before_o + incl2 - (h0 + h1);  // pairs before key hi
+  int key = -1, rank = 0;
+  if (pair_pos >= first && pair_pos < first + h0) {
+    key = hi;
+    rank = pair_pos - first;
+  } else if (pair_pos >= first + h0 && pair_pos < first + h0 + h1) {
+    key = hi - 1;
+    rank = pair_pos - first - h0;
+  }
+  const unsigned owner = __ballot_sync(full, key >= 0);
+  const int src = owner ? __ffs(owner) - 1 : 0;
+  key = __shfl_sync(full, key, src);
+  rank = __shfl_sync(full, rank, src);
+  // the rank-th pair (in id order) whose cost key is `key`
+  int found = 0;
+  for (int base = 0; base < pairs; base += 32) {
+    const int id = base + lane;
+    int c = -1;
+    if (id < pairs)
+      c = id < kTcCachedPairs ? cost[id]
+                              : tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq);
+    const unsigned m = __ballot_sync(full, c == key);
+    const int n = __popc(m);
+    if (rank < n) {
+      unsigned mm = m;
+      for (int r = 0; r < rank; ++r) mm &= mm - 1;  // drop the lower set bits
+      found = base + __ffs(mm) - 1;
+      break;
+    }
+    rank -= n;
+  }
+  return found;
+}
+
+// (sequence, row block, KV head) of grid position `pos`; `scratch` holds
+// kTcScratchInts ints of 16-byte aligned shared memory. Call with all
+// threads of the CTA. One round of metadata loads, then shared memory and
+// shuffles only: the whole CTA waits on this before any load is issued.
+__device__ __forceinline__ void tc_decode_unit(const PrefillParams& p, int pos, int* scratch,
+                                               int& s, int& rb, int& kvh) {
+  int* result = scratch + kTcHistInts;        // [2]
+  tc_build_hist(p, scratch);
   if (threadIdx.x < 32) {
-    const unsigned full = 0xffffffffu;
-    const int lane = threadIdx.x;
-    const int pair_pos = pos / p.num_kv_heads;
-    // Keys in descending order: lane l owns the chunk of keys
-    // [2048 - 64(l+1), 2048 - 64l), so lower lanes hold larger costs.
-    constexpr int kPerLane = kTcCostKeys / 32;
-    const int chunk_lo = kTcCostKeys - kPerLane * (lane + 1);
-    int chunk = 0;
-#pragma unroll
-    for (int k = 0; k < kPerLane / 4; ++k) {
-      const int4 h = reinterpret_cast<const int4*>(hist + tc_hist_slot(chunk_lo))[k];
-      chunk += (h.x + h.y) + (h.z + h.w);
-    }
-    // pairs in the chunks of lower lanes (larger keys): exclusive prefix sum
-    int incl = chunk;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int v = __shfl_up_sync(full, incl, d);
-      if (lane >= d) incl += v;
-    }
-    const unsigned own = __ballot_sync(full, pair_pos >= incl - chunk && pair_pos < incl);
-    const int o = own ? __ffs(own) - 1 : 0;
-    const int before_o = __shfl_sync(full, incl - chunk, o);
-    // inside chunk o, lane l takes keys hi = top - 2l and hi - 1 (descending)
-    const int hi = kTcCostKeys - 1 - kPerLane * o - 2 * lane;
-    const int h0 = hist[tc_hist_slot(hi)], h1 = hist[tc_hist_slot(hi - 1)];
-    int incl2 = h0 + h1;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int v = __shfl_up_sync(full, incl2, d);
-      if (lane >= d) incl2 += v;
-    }
-    const int first = before_o + incl2 - (h0 + h1);  // pairs before key hi
-    int key = -1, rank = 0;
-    if (pair_pos >= first && pair_pos < first + h0) {
-      key = hi;
-      rank = pair_pos - first;
-    } else if (pair_pos >= first + h0 && pair_pos < first + h0 + h1) {
-      key = hi - 1;
-      rank = pair_pos - first - h0;
-    }
-    const unsigned owner = __ballot_sync(full, key >= 0);
-    const int src = owner ? __ffs(owner) - 1 : 0;
-    key = __shfl_sync(full, key, src);
-    rank = __shfl_sync(full, rank, src);
-    // the rank-th pair (in id order) whose cost key is `key`
-    int found = 0;
-    for (int base = 0; base < pairs; base += 32) {
-      const int id = base + lane;
-      int c = -1;
-      if (id < pairs)
-        c = id < kTcCachedPairs ? cost[id]
-                                : tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq);
-      const unsigned m = __ballot_sync(full, c == key);
-      const int n = __popc(m);
-      if (rank < n) {
-        unsigned mm = m;
-        for (int r = 0; r < rank; ++r) mm &= mm - 1;  // drop the lower set bits
-        found = base + __ffs(mm) - 1;
-        break;
-      }
-      rank -= n;
-    }
-    if (lane == 0) {
+    const int found = tc_pair_at(p, scratch, pos / p.num_kv_heads, threadIdx.x);
+    if (threadIdx.x == 0) {
       result[0] = found;
       result[1] = pos % p.num_kv_heads;
     }
@@ -881,6 +899,605 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant (16-bit caches, Q by TMA): one CTA per SM walks a list
+// of units instead of one CTA per unit. The per-CTA work of the one-unit
+// kernel — tensor-memory allocation, barrier set-up, the unit decode, the
+// first Q/K/V loads, the last MMAs' drain and the epilogue — was a fixed
+// cost of about 10 us per unit, paid again for every short unit; here it is
+// paid once per CTA, and a unit's tail overlaps the next unit's start:
+//   * the producer loads the next unit's Q as soon as the current unit's
+//     last S MMAs have retired (q_empty), then keeps streaming K/V tiles of
+//     the next unit into the same rings (global stage counters);
+//   * the MMA warp issues the next unit's first S MMAs right after the
+//     current unit's last PV MMAs; before a Q tile's first PV MMA of a new
+//     unit it waits until that tile's epilogue has read O (o_free);
+//   * the softmax warps write a tile's output rows (epilogue) while the
+//     tensor core already computes the next unit's scores.
+// The units are the one-unit kernel's (sequence, row block, KV head), dealt
+// to the CTAs from the longest-first order in snake order: position
+// r * G + c on even rounds r and r * G + (G - 1 - c) on odd rounds for CTA c
+// of G, so a CTA that drew a long unit in one round draws a short one in the
+// next. Each CTA decodes its whole list once, before it starts.
+constexpr int kTcMaxUnitsPerCta = 64;
+constexpr int kTcPersistSmem = TcLayout<false>::kSmemBytes + 256;  // + the unit list
+
+__device__ __forceinline__ int tc_snake_pos(int k, int cta, int grid) {
+  return k * grid + ((k & 1) ? grid - 1 - cta : cta);
+}
+
+struct TcUnit {
+  int s, kvh, q_start, q_len, seq_len, ctx, tok_begin, n_a, n_b, n_total;
+};
+
+// Everything a role needs about unit `id` (= pair * num_kv_heads + KV head);
+// n_total = 0 for a row block past the sequence's chunk.
+__device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, int id) {
+  TcUnit u;
+  const int pair = id / p.num_kv_heads;
+  u.kvh = id - pair * p.num_kv_heads;
+  u.s = pair / p.blocks_per_seq;
+  const int rb = pair - u.s * p.blocks_per_seq;
+  u.q_start = __ldg(p.query_start_loc + u.s);
+  u.q_len = __ldg(p.query_start_loc + u.s + 1) - u.q_start;
+  u.seq_len = __ldg(p.seq_lens + u.s);
+  u.ctx = u.seq_len - u.q_len;
+  const int tpc = (kTcTiles * kTcRows) / p.group;
+  u.tok_begin = rb * tpc;
+  u.n_a = u.n_b = u.n_total = 0;
+  if (u.tok_begin >= u.q_len || u.seq_len <= 0) return u;
+  int n[kTcTiles];
+#pragma unroll
+  for (int x = 0; x < kTcTiles; ++x) {
+    n[x] = 0;
+    const int first_row = x * kTcRows;
+    if (first_row / p.group >= tpc || u.tok_begin + first_row / p.group >= u.q_len) continue;
+    const int last_row = min((x + 1) * kTcRows, tpc * p.group) - 1;
+    const int last_tok = min(u.q_len - 1, u.tok_begin + last_row / p.group);
+    const int kv_limit = min(u.seq_len, max(1, u.ctx + last_tok + 1));
+    n[x] = (kv_limit + kTcKv - 1) / kTcKv;
+  }
+  u.n_a = n[0];
+  u.n_b = n[1];
+  u.n_total = max(n[0], n[1]);
+  return u;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(tc_threads<false>(), 1)
+    paged_prefill_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                                       const __grid_constant__ CUtensorMap tmap_v,
+                                       const __grid_constant__ CUtensorMap tmap_q,
+                                       const PrefillParams p) {
+  using L = TcLayout<false>;
+  constexpr int kKSt = L::kKStages;
+  constexpr int kTcV0 = L::kV0;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  uint64_t* k_full = bars + 0;      // [3] TMA -> MMA
+  uint64_t* k_empty = bars + 3;     // [3] MMA (commit after the S MMAs) -> TMA
+  uint64_t* v_full = bars + 6;      // [2] TMA -> MMA
+  uint64_t* v_empty = bars + 8;     // [2] MMA (commit after the PV MMAs) -> TMA
+  uint64_t* s_full = bars + 10;     // [2] per Q tile: MMA (commit) -> softmax
+  uint64_t* p_ready = bars + 12;    // [2] per Q tile: P tokens 0-63 written -> MMA
+  uint64_t* o_done = bars + 14;     // [2] per Q tile: a unit's last PV retired -> epilogue
+  uint64_t* mma_drain = bars + 16;  // MMA (commit) -> MMA, before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* q_full = bars + 18;     // a unit's Q landed (TMA bytes) -> MMA
+  uint64_t* p_ready_hi = bars + 19; // [2] per Q tile: P tokens 64-127 written -> MMA
+  uint64_t* q_empty = bars + 21;    // a unit's last S MMAs retired -> producer (next Q)
+  uint64_t* o_free = bars + 22;     // [2] per Q tile: epilogue read O (128 arrivals) -> MMA
+  uint64_t* pv0_done = bars + 24;   // [2] per Q tile: a tile's first-half PV MMAs retired
+  int* units = reinterpret_cast<int*>(bars + 32);  // [kTcMaxUnitsPerCta] unit ids
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = p.num_seqs * p.blocks_per_seq * p.num_kv_heads;
+  int n_units = 0;
+  while (n_units < kTcMaxUnitsPerCta && tc_snake_pos(n_units, blockIdx.x, gridDim.x) < total)
+    ++n_units;
+
+  // ---- this CTA's unit list, from the longest-first order (Q region as scratch) ----
+  int* scratch = reinterpret_cast<int*>(smem + kTcQ);
+  tc_build_hist(p, scratch);
+  for (int k = warp; k < n_units; k += blockDim.x / 32) {
+    const int pos = tc_snake_pos(k, blockIdx.x, gridDim.x);
+    const int pair = tc_pair_at(p, scratch, pos / p.num_kv_heads, lane);
+    if (lane == 0) units[k] = pair * p.num_kv_heads + pos % p.num_kv_heads;
+  }
+
+  const uint32_t sbase = smem_u32(smem);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kKSt; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
+    }
+    for (int i = 0; i < kTcVStages; ++i) {
+      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_empty[i]), 1);
+    }
+    for (int x = 0; x < kTcTiles; ++x) {
+      mbar_init(smem_u32(&s_full[x]), 1);
+      mbar_init(smem_u32(&p_ready[x]), kTcRows);
+      mbar_init(smem_u32(&p_ready_hi[x]), kTcRows);
+      mbar_init(smem_u32(&o_done[x]), 1);
+      mbar_init(smem_u32(&o_free[x]), kTcRows);
+      mbar_init(smem_u32(&pv0_done[x]), 1);
+    }
+    mbar_init(smem_u32(mma_drain), 1);
+    mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_empty), 1);
+    mbar_init_fence();
+  }
+  if (warp == kTcMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
+    tmem_relinquish();
+  }
+  // the unit list, barriers and TMEM address are visible after this; the
+  // scratch (Q region) is free for the first unit's Q
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  bool ok = true;
+
+  if (warp == kTcProducerWarp) {
+    // ------------------------------------------------------------ producer --
+    // Per unit: its Q (once the previous unit's S MMAs retired), then K0, K1,
+    // (V_j, K_{j+2}) ... as in the one-unit kernel; stages and phases count
+    // the K and V tiles of all units in order.
+    int issued_k = 0, issued_v = 0, units_q = 0;
+    int gk = 0, gv = 0;  // first global K / V tile index of the current unit
+    for (int k = 0; k < n_units && ok; ++k) {
+      const TcUnit U = tc_unit(p, units[k]);
+      if (U.n_total == 0) continue;
+      const int max_page_idx = (U.seq_len - 1) / p.block_size;
+      TilePages pages{p.block_tables + (int64_t)U.s * p.block_table_stride, max_page_idx,
+                      p.block_size, lane, 0, 0};
+      pages.init();
+      auto load = [&](bool is_v, int j) -> bool {
+        const int g = (is_v ? gv : gk) + j;
+        const int nst = is_v ? kTcVStages : kKSt;
+        const int st = g % nst;
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        if (g >= nst) {
+          const bool got = mbar_wait(smem_u32(&empty[st]), ((g / nst) - 1) & 1);
+          if (!__all_sync(0xffffffffu, got)) return false;
+        }
+        const uint32_t bar = smem_u32(is_v ? &v_full[st] : &k_full[st]);
+        if (lane == 0) mbar_arrive_expect_tx(bar, kTcTileBytes);
+        __syncwarp();
+        const int page = pages.page(j);
+        if (lane < kTcKv / kTileTokens) {
+          const int tok = j * kTcKv + lane * kTileTokens;
+          // past the sequence end: the last page (any valid one), masked later
+          const int row = tok / p.block_size > max_page_idx ? 0 : tok % p.block_size;
+          if (page < 0 || page >= p.num_blocks)
+            report_status(p.status, B200_STATUS_PAGE_OUT_OF_RANGE);
+          const uint32_t dst =
+              sbase + (is_v ? kTcV0 : kTcK0) + st * kTcTileBytes + lane * kHalfTileBytes;
+          const CUtensorMap* map = is_v ? &tmap_v : &tmap_k;
+          tma_load_4d(dst, map, bar, 0, U.kvh, row, page);
+          tma_load_4d(dst + kTcHalf, map, bar, 64, U.kvh, row, page);
+        }
+        if (is_v) issued_v = g + 1; else issued_k = g + 1;
+        return true;
+      };
+      // the Q tiles are free once every S MMA of the previous unit retired
+      if (units_q > 0) {
+        const bool got = mbar_wait(smem_u32(q_empty), (units_q - 1) & 1);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+      }
+      if (lane == 0) {
+        // per tile and d half one box of group heads x 128 / group tokens,
+        // which is the tile's 128 (token, head) rows in order
+        const int tpt = kTcRows / p.group;
+        mbar_arrive_expect_tx(smem_u32(q_full), kTcTiles * kTcTileBytes);
+        for (int x = 0; x < kTcTiles; ++x)
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sbase + kTcQ + x * kTcTileBytes + h * kTcHalf, &tmap_q,
+                        smem_u32(q_full), h * 64, U.kvh * p.group,
+                        U.q_start + U.tok_begin + x * tpt);
+      }
+      __syncwarp();
+      ++units_q;
+      const int n = U.n_total;
+      for (int j = 0; j < min(2, n) && ok; ++j) ok = load(false, j);
+      for (int j = 0; j < n && ok; ++j) {
+        pages.advance(j);
+        ok = load(true, j);
+        if (ok && j + 2 < n) ok = load(false, j + 2);
+      }
+      gk += n;
+      gv += n;
+    }
+    if (!ok) {
+      if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+      // loads still in flight land before the CTA exits (bounded waits)
+      for (int g = max(0, issued_k - kKSt); g < issued_k; ++g)
+        mbar_wait(smem_u32(&k_full[g % kKSt]), (g / kKSt) & 1);
+      for (int g = max(0, issued_v - kTcVStages); g < issued_v; ++g)
+        mbar_wait(smem_u32(&v_full[g % kTcVStages]), (g / kTcVStages) & 1);
+      if (units_q > 0) mbar_wait(smem_u32(q_full), (units_q - 1) & 1);
+    }
+  } else if (warp == kTcMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      constexpr bool kBf16 = Elem<T>::kDtype == B200_DTYPE_BFLOAT16;
+      const uint32_t idesc_s = f16_instr_desc(kTcRows, kTcKv, kBf16, false);
+      const uint32_t idesc_pv = f16_instr_desc(kTcRows, kHeadDim, kBf16, true);
+      auto kmajor = [&](uint32_t addr, int k) {  // K-major, 16-element k-step k
+        return smem_desc(addr + (k >> 2) * kTcHalf + (k & 3) * 32, 16, 1024);
+      };
+      auto issue_s = [&](int x, int g) {  // S_X = Q_X K(g)^T
+        const uint32_t qbase = sbase + kTcQ + x * 2 * kTcHalf;
+        const uint32_t kbase = sbase + kTcK0 + (g % kKSt) * kTcTileBytes;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k)
+          umma_f16(tmem_base + x * 256, kmajor(qbase, k), kmajor(kbase, k), idesc_s,
+                   k > 0 ? 1u : 0u);
+        umma_commit(smem_u32(&s_full[x]));
+      };
+      // O_X (+)= P_X V(g), k-steps [k0, k0 + 4): the 64 KV tokens of one half of P
+      auto issue_pv = [&](int x, int g, int k0, bool first_of_unit) {
+        const uint32_t vbase = sbase + kTcV0 + (g % kTcVStages) * kTcTileBytes;
+        const uint32_t tP = tmem_base + x * 256;  // P (16-bit, packed) over S
+#pragma unroll
+        for (int k = k0; k < k0 + kTcKv / 32; ++k)
+          umma_f16_ts(tmem_base + x * 256 + 128, tP + k * 8,
+                      smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
+                      (!first_of_unit || k > 0) ? 1u : 0u);
+      };
+      int k_ready = -1, v_ready = -1;  // highest global tiles whose full phase was observed
+      auto wait_k = [&](int g) {
+        if (g <= k_ready) return true;
+        if (!mbar_wait(smem_u32(&k_full[g % kKSt]), (g / kKSt) & 1)) return false;
+        k_ready = g;
+        return true;
+      };
+      auto wait_v = [&](int g) {
+        if (g <= v_ready) return true;
+        if (!mbar_wait(smem_u32(&v_full[g % kTcVStages]), (g / kTcVStages) & 1)) return false;
+        v_ready = g;
+        return true;
+      };
+      int gk = 0, gv = 0, units_q = 0;
+      int ts[kTcTiles] = {0, 0};  // tile steps per Q tile (s_full / p_ready phases)
+      int ep[kTcTiles] = {0, 0};  // units with rows per Q tile (o_done / o_free phases)
+      for (int k = 0; k < n_units && ok; ++k) {
+        const TcUnit U = tc_unit(p, units[k]);
+        if (U.n_total == 0) continue;
+        const int nx[kTcTiles] = {U.n_a, U.n_b};
+        const int n = U.n_total;
+        // S of tile 0 for both Q tiles, once this unit's Q landed
+        if (!mbar_wait(smem_u32(q_full), units_q & 1) || !wait_k(gk)) {
+          ok = false;
+          break;
+        }
+        ++units_q;
+        for (int x = 0; x < kTcTiles; ++x)
+          if (nx[x] > 0) issue_s(x, gk);
+        umma_commit(smem_u32(&k_empty[gk % kKSt]));  // after every S of tile 0
+        if (n == 1) umma_commit(smem_u32(q_empty));   // the unit's last S MMAs
+        for (int j = 0; j < n && ok; ++j) {
+          for (int x = 0; x < kTcTiles && ok; ++x) {
+            if (j >= nx[x]) continue;
+            if (!mbar_wait(smem_u32(&p_ready[x]), ts[x] & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after_sync();
+            if (j == 0 && ep[x] > 0) {
+              // the first PV of a unit overwrites O_X: the previous unit's
+              // epilogue must have read it
+              if (!mbar_wait(smem_u32(&o_free[x]), (ep[x] - 1) & 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after_sync();
+            }
+            if (!wait_v(gv + j)) {
+              ok = false;
+              break;
+            }
+            issue_pv(x, gv + j, 0, j == 0);
+            umma_commit(smem_u32(&pv0_done[x]));  // for a softmax that must rescale O
+            if (!mbar_wait(smem_u32(&p_ready_hi[x]), ts[x] & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after_sync();
+            issue_pv(x, gv + j, kTcKv / 32, false);
+            if (j == nx[x] - 1) umma_commit(smem_u32(&o_done[x]));
+            if (j + 1 < nx[x]) {
+              if (!wait_k(gk + j + 1)) {
+                ok = false;
+                break;
+              }
+              issue_s(x, gk + j + 1);
+            }
+            ++ts[x];
+          }
+          if (!ok) break;
+          umma_commit(smem_u32(&v_empty[(gv + j) % kTcVStages]));  // after every PV of tile j
+          if (j + 1 < n) umma_commit(smem_u32(&k_empty[(gk + j + 1) % kKSt]));
+          if (j + 2 == n) umma_commit(smem_u32(q_empty));  // S of the last tile issued above
+        }
+        for (int x = 0; x < kTcTiles; ++x) ep[x] += nx[x] > 0 ? 1 : 0;
+        gk += n;
+        gv += n;
+      }
+      if (!ok) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(smem_u32(mma_drain));
+      mbar_wait(smem_u32(mma_drain), 0);
+    }
+    __syncwarp();
+  } else if (warp < 8) {
+    // ------------------------------------------------------- softmax warps --
+    const int x_tile = warp >> 2;       // Q tile of this warpgroup
+    const int t = threadIdx.x & 127;    // row within the Q tile = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + x_tile * 256 + lane_off;
+    const uint32_t tO = tS + 128;
+    const float kNegInf = -INFINITY;
+    const float scale = p.scale_log2;
+    const int group = p.group;
+    const int tpc = (kTcTiles * kTcRows) / group;
+    int ts = 0, ep = 0, gv = 0;
+    for (int k = 0; k < n_units && ok; ++k) {
+      const TcUnit U = tc_unit(p, units[k]);
+      const int my_tiles = x_tile ? U.n_b : U.n_a;
+      if (my_tiles == 0) {
+        gv += U.n_total;
+        continue;
+      }
+      const int seq_len = U.seq_len;
+      int row_token = -1, row_head = 0, qpos = -1;
+      {
+        const int r = x_tile * kTcRows + t;  // rows are (token, q head of the group) pairs
+        const int tl = r / group;
+        if (tl < tpc && U.tok_begin + tl < U.q_len) {
+          row_token = U.tok_begin + tl;
+          row_head = U.kvh * group + (r - tl * group);
+          qpos = U.ctx + row_token;
+        }
+      }
+      float m_used = kNegInf, l = 0.f;
+      // P of the 64 columns [64h, 64h + 64) with exponent base -neg_base:
+      // packed 16-bit pairs, their sum and the raw maximum of the visible scores
+      auto exp_half = [&](auto masked, int h, float neg_base, int lim, uint32_t (&pk)[2][16],
+                          float& sum, float& mraw) {
+        constexpr bool kMasked = decltype(masked)::value;
+        const uint64_t scale2 = f2(scale, scale), base2 = f2(neg_base, neg_base);
+        uint64_t sk2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+        float mk[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * h + cc;
+          float sv[32];
+          tmem_ld32(tS + c * 32, sv);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const bool v0 = !kMasked || c * 32 + 2 * i < lim;
+            const bool v1 = !kMasked || c * 32 + 2 * i + 1 < lim;
+            mk[(2 * i) & 3] = fmaxf(mk[(2 * i) & 3], v0 ? sv[2 * i] : kNegInf);
+            mk[(2 * i + 1) & 3] = fmaxf(mk[(2 * i + 1) & 3], v1 ? sv[2 * i + 1] : kNegInf);
+            float x0, x1;
+            f2_split(f2_fma(f2(sv[2 * i], sv[2 * i + 1]), scale2, base2), x0, x1);
+            float p0 = ex2_approx(x0);
+            float p1 = ex2_approx(x1);
+            if (kMasked) {
+              p0 = v0 ? p0 : 0.f;
+              p1 = v1 ? p1 : 0.f;
+            }
+            sk2[i & 1] = f2_add(sk2[i & 1], f2(p0, p1));
+            pk[cc][i] = pack2<T>(p0, p1);
+          }
+        }
+        float s0, s1, s2, s3;
+        f2_split(sk2[0], s0, s1);
+        f2_split(sk2[1], s2, s3);
+        sum = (s0 + s1) + (s2 + s3);
+        mraw = fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3]));
+      };
+      auto rescale_o = [&](float a) {  // warp-collective; a = 1 leaves a row as it is
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tO + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= a;
+          tmem_st32(tO + c * 32, ov);
+        }
+      };
+      for (int j = 0; j < my_tiles; ++j) {
+        const bool got = mbar_wait(smem_u32(&s_full[x_tile]), ts & 1);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const int kbase = j * kTcKv;
+        // columns [0, lim) of this tile are visible to this row
+        const int lim = min(qpos - kbase + 1, seq_len - kbase);
+        const bool need_mask = lim < kTcKv;
+        // exp_half holds warp-collective tensor-memory loads: the masked or
+        // unmasked variant is chosen for the whole warp (a row without a mask
+        // has lim >= 128, so masking leaves it unchanged)
+        const bool warp_mask = __any_sync(0xffffffffu, need_mask);
+        if (kbase + kTcKv > seq_len) {
+          // Last KV tile: V rows past the sequence end may hold never-written
+          // cache slots (possibly NaN) and P = 0 does not cancel NaN. Both
+          // warpgroups write the same zeros, each before its own PV.
+          const int g = gv + j;
+          const bool landed = mbar_wait(smem_u32(&v_full[g % kTcVStages]), (g / kTcVStages) & 1);
+          if (!__all_sync(0xffffffffu, landed)) {
+            ok = false;
+            break;
+          }
+          if (kbase + t >= seq_len) {
+            uint8_t* vrow = smem + kTcV0 + (g % kTcVStages) * kTcTileBytes + t * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(vrow + kTcHalf + c * 16) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        if (j == 0) {
+          // ---- a unit's first tile: the exact maximum first (there is no
+          // running base yet), then the exponentials ----
+          float mk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mk[i] = kNegInf;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float sv[64];
+            tmem_ld64(tS + c * 64, sv);
+            if (need_mask) {
+#pragma unroll
+              for (int i = 0; i < 64; ++i)
+                mk[i & 7] = fmaxf(mk[i & 7], c * 64 + i < lim ? sv[i] : kNegInf);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 64; ++i) mk[i & 7] = fmaxf(mk[i & 7], sv[i]);
+            }
+          }
+          // the softmax scale is positive, so it commutes with the maximum
+          const float m_raw = fmaxf(fmaxf(fmaxf(mk[0], mk[1]), fmaxf(mk[2], mk[3])),
+                                    fmaxf(fmaxf(mk[4], mk[5]), fmaxf(mk[6], mk[7])));
+          m_used = m_raw == kNegInf ? kNegInf : m_raw * scale;
+          const float nb = m_used == kNegInf ? 0.f : -m_used;
+          float tile_sum = 0.f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t pk[2][16];
+            float sh, mr;
+            if (warp_mask) exp_half(std::true_type{}, h, nb, lim, pk, sh, mr);
+            else exp_half(std::false_type{}, h, nb, lim, pk, sh, mr);
+            tile_sum += sh;
+            // P over S: the half's 64 values -> 32 columns at 32h, which only
+            // overlap S columns this row has already read
+            tmem_st16(tS + (2 * h) * 16, pk[0]);
+            tmem_st16(tS + (2 * h + 1) * 16, pk[1]);
+            tmem_wait_st();
+            tc_fence_before_sync();
+            mbar_arrive(smem_u32(h == 0 ? &p_ready[x_tile] : &p_ready_hi[x_tile]));
+          }
+          l = tile_sum;
+        } else {
+          // ---- later tiles: one pass with the running base, keeping each
+          // half's maximum; only a half whose maximum exceeds the base by
+          // more than the threshold (rare) is done again with a new base ----
+          float tile_sum = 0.f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t pk[2][16];
+            float sh, mr;
+            const float nb = m_used == kNegInf ? 0.f : -m_used;
+            if (warp_mask) exp_half(std::true_type{}, h, nb, lim, pk, sh, mr);
+            else exp_half(std::false_type{}, h, nb, lim, pk, sh, mr);
+            const float mh = mr == kNegInf ? kNegInf : mr * scale;
+            const bool need = mh > m_used + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, need)) {
+              const float m_new = need ? mh : m_used;
+              const float a = need ? fast_exp2(m_used - m_new) : 1.f;
+              if (h == 1) {
+                // half 0 of this tile is with the MMA warp: O must hold it
+                // before it is rescaled
+                const bool got0 = mbar_wait(smem_u32(&pv0_done[x_tile]), ts & 1);
+                if (!__all_sync(0xffffffffu, got0)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after_sync();
+              }
+              // O_X holds every earlier contribution (S_X(j) done implies
+              // PV_X(j-1) done; for h = 1 also half 0 of this tile)
+              rescale_o(a);
+              l *= a;
+              tile_sum *= a;
+              m_used = m_new;
+              const float nb2 = m_used == kNegInf ? 0.f : -m_used;
+              if (warp_mask) exp_half(std::true_type{}, h, nb2, lim, pk, sh, mr);
+              else exp_half(std::false_type{}, h, nb2, lim, pk, sh, mr);
+            }
+            tile_sum += sh;
+            tmem_st16(tS + (2 * h) * 16, pk[0]);
+            tmem_st16(tS + (2 * h + 1) * 16, pk[1]);
+            tmem_wait_st();
+            tc_fence_before_sync();
+            mbar_arrive(smem_u32(h == 0 ? &p_ready[x_tile] : &p_ready_hi[x_tile]));
+          }
+          if (!ok) break;
+          l += tile_sum;
+        }
+        ++ts;
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l to the output rows, then O_X is free ----
+      const bool done = mbar_wait(smem_u32(&o_done[x_tile]), ep & 1);
+      if (!__all_sync(0xffffffffu, done)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      // O / l packed to T in two 64-column halves (bounded register use);
+      // the row's output stays in registers until O_X is released
+      uint4 packed[16];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t ob[2][32];
+        tmem_ld32_issue(tO + h * 64, ob[0]);
+        tmem_ld32_issue(tO + h * 64 + 32, ob[1]);
+        tmem_wait_ld32(ob[0]);
+        tmem_wait_ld32(ob[1]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const float* ov = reinterpret_cast<const float*>(ob[c]);
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 pk;
+            pk.x = pack2<T>(ov[q8 * 8 + 0] * inv_l, ov[q8 * 8 + 1] * inv_l);
+            pk.y = pack2<T>(ov[q8 * 8 + 2] * inv_l, ov[q8 * 8 + 3] * inv_l);
+            pk.z = pack2<T>(ov[q8 * 8 + 4] * inv_l, ov[q8 * 8 + 5] * inv_l);
+            pk.w = pack2<T>(ov[q8 * 8 + 6] * inv_l, ov[q8 * 8 + 7] * inv_l);
+            packed[(h * 2 + c) * 4 + q8] = pk;
+          }
+        }
+      }
+      // every read of O_X has landed in registers: the next unit may overwrite it
+      tc_fence_before_sync();
+      mbar_arrive(smem_u32(&o_free[x_tile]));
+      if (row_token >= 0) {
+        uint4* orow = reinterpret_cast<uint4*>(
+            reinterpret_cast<T*>(p.out) + (int64_t)(U.q_start + row_token) * p.out_token_stride +
+            (int64_t)row_head * p.out_head_stride);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) orow[i] = packed[i];
+      }
+      ++ep;
+      gv += U.n_total;
+    }
+    if (!ok && lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == kTcMmaWarp) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+}
+
 template <typename T, bool kFp8>
 static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
                                    const CUtensorMap& mq, const CUtensorMap& mo,
@@ -899,6 +1516,23 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   q.blocks_per_seq = blocks;
   const int64_t units = (int64_t)blocks * num_kv_heads * num_seqs;
   if (units > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if constexpr (!kFp8) {
+    if (q.q_tma) {
+      // persistent: one CTA per SM (at most kTcMaxUnitsPerCta units each)
+      auto pkernel = paged_prefill_tc_persistent_kernel<T>;
+      e = ensure_smem_attr(reinterpret_cast<const void*>(pkernel), kTcPersistSmem);
+      if (e != cudaSuccess) return e;
+      int dev = 0, sms = 0;
+      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+      int64_t grid = units < sms ? units : sms;
+      const int64_t min_grid = (units + kTcMaxUnitsPerCta - 1) / kTcMaxUnitsPerCta;
+      if (grid < min_grid) grid = min_grid;
+      pkernel<<<(unsigned)grid, tc_threads<false>(), kTcPersistSmem, stream>>>(mk, mv, mq, q);
+      return cudaGetLastError();
+    }
+  }
   kernel<<<(unsigned)units, tc_threads<kFp8>(), kSmem, stream>>>(mk, mv, mq, mo, q);
   return cudaGetLastError();
 }
