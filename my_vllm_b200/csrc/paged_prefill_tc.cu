@@ -1131,26 +1131,39 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
       constexpr bool kBf16 = Elem<T>::kDtype == B200_DTYPE_BFLOAT16;
       const uint32_t idesc_s = f16_instr_desc(kTcRows, kTcKv, kBf16, false);
       const uint32_t idesc_pv = f16_instr_desc(kTcRows, kHeadDim, kBf16, true);
-      auto kmajor = [&](uint32_t addr, int k) {  // K-major, 16-element k-step k
-        return smem_desc(addr + (k >> 2) * kTcHalf + (k & 3) * 32, 16, 1024);
+      // Shared-memory descriptors are built once: a k-step or a ring stage
+      // only moves the start-address field (bits 0-13, address / 16, no carry
+      // below 256 KiB), so each MMA adds a constant to a precomputed base
+      // instead of rebuilding the descriptor (the single issuing thread is
+      // the pipeline's serial resource).
+      uint64_t qdesc[kTcTiles], kdesc[kKSt], vdesc[kTcVStages];
+#pragma unroll
+      for (int x = 0; x < kTcTiles; ++x) qdesc[x] = smem_desc(sbase + kTcQ + x * 2 * kTcHalf, 16, 1024);
+#pragma unroll
+      for (int st = 0; st < kKSt; ++st) kdesc[st] = smem_desc(sbase + kTcK0 + st * kTcTileBytes, 16, 1024);
+#pragma unroll
+      for (int st = 0; st < kTcVStages; ++st)
+        vdesc[st] = smem_desc(sbase + kTcV0 + st * kTcTileBytes, kTcHalf, 1024);
+      // K-major operand, 16-element k-step k: (k / 4) 64-element halves + (k % 4) 32-byte steps
+      auto kstep = [](int k) -> uint64_t {
+        return static_cast<uint64_t>(((k >> 2) * kTcHalf + (k & 3) * 32) >> 4);
       };
       auto issue_s = [&](int x, int g) {  // S_X = Q_X K(g)^T
-        const uint32_t qbase = sbase + kTcQ + x * 2 * kTcHalf;
-        const uint32_t kbase = sbase + kTcK0 + (g % kKSt) * kTcTileBytes;
+        const uint64_t kd = kdesc[g % kKSt];
 #pragma unroll
         for (int k = 0; k < kHeadDim / 16; ++k)
-          umma_f16(tmem_base + x * 256, kmajor(qbase, k), kmajor(kbase, k), idesc_s,
+          umma_f16(tmem_base + x * 256, qdesc[x] + kstep(k), kd + kstep(k), idesc_s,
                    k > 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[x]));
       };
       // O_X (+)= P_X V(g), k-steps [k0, k0 + 4): the 64 KV tokens of one half of P
       auto issue_pv = [&](int x, int g, int k0, bool first_of_unit) {
-        const uint32_t vbase = sbase + kTcV0 + (g % kTcVStages) * kTcTileBytes;
+        const uint64_t vd = vdesc[g % kTcVStages];
         const uint32_t tP = tmem_base + x * 256;  // P (16-bit, packed) over S
 #pragma unroll
         for (int k = k0; k < k0 + kTcKv / 32; ++k)
           umma_f16_ts(tmem_base + x * 256 + 128, tP + k * 8,
-                      smem_desc(vbase + k * 16 * 128, kTcHalf, 1024), idesc_pv,
+                      vd + static_cast<uint64_t>((k * 16 * 128) >> 4), idesc_pv,
                       (!first_of_unit || k > 0) ? 1u : 0u);
       };
       int k_ready = -1, v_ready = -1;  // highest global tiles whose full phase was observed
