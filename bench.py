@@ -774,10 +774,13 @@ def measure_config3(device, steps, warmup, fp8=False):
     step_bytes = prefill_kv_bytes + decode_kv_bytes + w.append_bytes()
     stream = torch.cuda.current_stream(device)
 
+    prefill_ws = backend._prefill_workspace_for(device)  # the backend's split-KV workspace
+
     def prefill():
         ops.paged_prefill(w.q[:P], w.k_cache, w.v_cache, md.block_tables[:nP],
                           md.seq_lens[:nP], md.query_start_loc[: nP + 1], out[:P],
-                          common.max_q_len, backend.softmax_scale, num_seqs=nP, **scales)
+                          common.max_q_len, backend.softmax_scale, num_seqs=nP,
+                          workspace=prefill_ws, **scales)
 
     def decode():
         ops.paged_decode(w.q[P:], w.k_cache, w.v_cache, md.block_tables[nP:],
@@ -893,9 +896,10 @@ def measure_prefill_long(device, steps, warmup, seqs=4, tokens=8192):
     out = torch.empty_like(w.q)
     stream = torch.cuda.current_stream(device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
+    ws = torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=device)
     ms = event_ms(lambda: ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables,
                                             w.seq_lens, w.query_start_loc, out, tokens,
-                                            HEAD_DIM ** -0.5, status=status),
+                                            HEAD_DIM ** -0.5, status=status, workspace=ws),
                   steps, warmup, stream)
     if int(status.item()):
         raise RuntimeError(f"prefill reported status {int(status.item())}")

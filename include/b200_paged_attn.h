@@ -320,11 +320,20 @@ B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_seq_stride,
  * of q/out and seq_lens[s] KV tokens (the new ones included, already
  * appended to the cache). Query row i of a q_len-row chunk attends to KV
  * positions < seq_len - q_len + i + 1 (bottom-right causal mask,
- * tests/test_attention_backend.py:686-693).
+ * tests/test_attention_backend.py:660-699).
  * max_q_len bounds the chunk length (host value from the metadata).
  * num_q_tokens is the number of rows q holds: Q tiles may be fetched, and
  * output tiles stored, as whole boxes through tensor maps bounded by it, so
  * both q and out must hold at least num_q_tokens rows.
+ * workspace (optional, NULL = none): b200_paged_prefill_workspace_bytes()
+ * of device memory, 256-byte aligned. With it, 16-bit caches whose GQA group
+ * divides 128 split the KV range of units much longer than the batch's
+ * average work per SM over several CTAs (partial results merged in the
+ * workspace): a long chunk on a long cached prefix then uses the whole GPU.
+ * Zero the workspace once before its first use; a launch leaves its
+ * counters zero again, unless it reports an error in *status, after which
+ * the workspace must be zeroed again. Launches that share one workspace
+ * must not overlap on the GPU.
  * Replaces BatchPrefillWithPagedKVCacheWrapper.run as called from
  * FlashInferBackend.forward (attention_backend.py:992-994, 1014-1019).
  */
@@ -334,8 +343,12 @@ B200_API int b200_paged_prefill(const void* q, int64_t q_token_stride,
                        const int32_t* seq_lens, const int32_t* query_start_loc,
                        int32_t num_seqs, int32_t num_q_tokens, int32_t max_q_len,
                        int32_t num_q_heads, void* out, int64_t out_token_stride,
-                       int64_t out_head_stride, float softmax_scale,
-                       int32_t* status, void* stream);
+                       int64_t out_head_stride, float softmax_scale, void* workspace,
+                       int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* Bytes of the optional b200_paged_prefill workspace (split-KV partial
+ * results). No counterpart in the reference (FlashInfer keeps its own). */
+B200_API int64_t b200_paged_prefill_workspace_bytes(void);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "b200_paged_decode_plan",
     "b200_paged_decode",
     "b200_paged_prefill",
+    "b200_paged_prefill_workspace_bytes",
     "b200_paged_decode_noalloc",
 )
 
@@ -139,10 +140,11 @@ _SIGNATURES = {
     "b200_paged_prefill": (
         [
             _VP, _I64, _I64, ctypes.POINTER(PagedCache), _VP, _I64, _VP, _VP, _I32,
-            _I32, _I32, _I32, _VP, _I64, _I64, _F32, _VP, _VP,
+            _I32, _I32, _I32, _VP, _I64, _I64, _F32, _VP, _I64, _VP, _VP,
         ],
         _I32,
     ),
+    "b200_paged_prefill_workspace_bytes": ([], _I64),
 }
 
 _lock = threading.Lock()

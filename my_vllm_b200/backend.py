@@ -142,6 +142,7 @@ class B200PagedBackend(AttentionBackend):
         self._route_counts = {route.value: 0 for route in AttentionRoute}
         self._output_buffer: torch.Tensor | None = None
         self._workspace: torch.Tensor | None = None
+        self._prefill_workspace: torch.Tensor | None = None
         self._status: torch.Tensor | None = None
         self._active_graph_state: B200DecodeGraphState | None = None
         self._side_streams: dict[torch.device, torch.cuda.Stream] = {}
@@ -202,6 +203,8 @@ class B200PagedBackend(AttentionBackend):
         bits = int(self._status.item())
         if bits:
             self._status.zero_()
+            if self._prefill_workspace is not None:  # a failed launch may leave counters set
+                self._prefill_workspace.zero_()
             raise RuntimeError(f"B200 attention kernels reported: {_native.describe_status(bits)}")
 
     # -------------------------------------------------------------- metadata --
@@ -272,6 +275,16 @@ class B200PagedBackend(AttentionBackend):
         if ws is None or ws.numel() < nbytes or ws.device != device:
             ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
             self._workspace = ws
+        return ws
+
+    def _prefill_workspace_for(self, device: torch.device) -> torch.Tensor:
+        """The backend's split-KV prefill workspace (allocated once per device;
+        the prefill launches of one backend run in order on one stream)."""
+        ws = self._prefill_workspace
+        if ws is None or ws.device != device:
+            # zeroed once: every launch leaves its split counters at zero
+            ws = torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=device)
+            self._prefill_workspace = ws
         return ws
 
     def _get_reusable_attention_output(self, q: torch.Tensor) -> torch.Tensor:
@@ -361,7 +374,7 @@ class B200PagedBackend(AttentionBackend):
                 q[:P], k_cache, v_cache, block_tables[:nP], metadata.seq_lens[:nP],
                 metadata.query_start_loc[: nP + 1], output[:P], common.max_q_len,
                 self.softmax_scale, num_seqs=nP, k_scale=k_scale, v_scale=v_scale,
-                status=status,
+                status=status, workspace=self._prefill_workspace_for(q.device),
             )
 
         def decode():

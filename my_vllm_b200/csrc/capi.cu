@@ -568,13 +568,16 @@ int b200_paged_decode(const void* q, int64_t q_seq_stride, int64_t q_head_stride
   return B200_OK;
 }
 
+int64_t b200_paged_prefill_workspace_bytes(void) { return b200::prefill_workspace_bytes(); }
+
 int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_stride,
                        const b200_paged_cache* cache, const int32_t* block_tables,
                        int64_t block_table_stride, const int32_t* seq_lens,
                        const int32_t* query_start_loc, int32_t num_seqs, int32_t num_q_tokens,
                        int32_t max_q_len, int32_t num_q_heads, void* out,
                        int64_t out_token_stride, int64_t out_head_stride, float softmax_scale,
-                       int32_t* status, void* stream) {
+                       void* workspace, int64_t workspace_bytes, int32_t* status,
+                       void* stream) {
   g_last_error.clear();
   int rc = validate_cache(cache);
   if (rc != B200_OK) return rc;
@@ -592,6 +595,13 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
       (q_token_stride | q_head_stride | out_token_stride | out_head_stride) & 7)
     return fail(B200_ERR_INVALID_ARGUMENT,
                 "q/out must be 16-byte aligned with strides that are multiples of 8");
+  if (workspace != nullptr) {
+    if (workspace_bytes < b200::prefill_workspace_bytes())
+      return fail(B200_ERR_INVALID_ARGUMENT,
+                  "prefill workspace smaller than b200_paged_prefill_workspace_bytes()");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+      return fail(B200_ERR_INVALID_ARGUMENT, "prefill workspace must be 256-byte aligned");
+  }
   CUtensorMap mk, mv;
   if ((rc = cache_tensor_map(cache->k_cache, *cache, &mk)) != B200_OK) return rc;
   if ((rc = cache_tensor_map(cache->v_cache, *cache, &mv)) != B200_OK) return rc;
@@ -614,6 +624,17 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.k_scale = cache->k_scale;
   p.v_scale = cache->v_scale;
   p.status = status;
+  // split-KV of long units needs the workspace (tickets, then part records)
+  p.split_records = nullptr;
+  p.split_tickets = nullptr;
+  p.split_cap = 0;
+  p.num_sms = 0;
+  if (workspace != nullptr) {
+    p.split_tickets = static_cast<int*>(workspace);
+    p.split_records = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                               b200::prefill_split_ticket_bytes());
+    p.split_cap = b200::kPrefillSplitCap;
+  }
   // Q by TMA when a tile's rows are one box of the q tensor: a GQA group that
   // divides 128 (FP8 caches convert the landed Q to fp16 in shared memory).
   CUtensorMap mq;

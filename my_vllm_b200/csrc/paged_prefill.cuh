@@ -33,7 +33,23 @@ struct PrefillParams {
   int o_tma;           // 1: Q tiles whose rows all belong to the sequence leave by a
                        // TMA store through the out tensor map; 0: per-thread stores
   int32_t* status;
+  // Split-KV (persistent kernel, 16-bit caches): a unit costlier than the
+  // average per-SM work is cut into KV parts on different CTAs; the part
+  // that finishes last merges the others' partial records. Off when
+  // split_cap == 0 (no workspace).
+  float* split_records;  // [split_cap][2 Q tiles][130][128 rows]: O columns, m, l
+  int* split_tickets;    // [split_cap][2 Q tiles], zeroed before each launch
+  int split_cap;         // part records the workspace holds
+  int num_sms;
 };
+
+// Part records of the prefill split-KV workspace and its size.
+constexpr int kPrefillSplitCap = 256;
+constexpr int64_t kPrefillRecordFloats = 2 * 130 * 128;
+constexpr int64_t prefill_split_ticket_bytes() { return (kPrefillSplitCap * 2 * 4 + 255) / 256 * 256; }
+constexpr int64_t prefill_workspace_bytes() {
+  return prefill_split_ticket_bytes() + kPrefillSplitCap * kPrefillRecordFloats * 4;
+}
 
 // tcgen05 / TMEM prefill: 128 packed (query token, q head of the group) rows
 // per CTA on UMMA M = 128 tiles, so the GQA heads of a KV head share every

@@ -265,19 +265,21 @@ struct TilePages {
   const int32_t* bt_row;
   int max_page_idx, block_size, lane;
   int even, odd;
+  int g0 = 0;  // first group: tile g0 * 4 is the first the caller streams (KV parts)
 
   __device__ __forceinline__ int fetch(int g) const {
     const int tok = (g * 4 + (lane >> 3)) * kTcKv + (lane & 7) * kTileTokens;
     return __ldg(bt_row + min(tok / block_size, max_page_idx));
   }
   __device__ __forceinline__ void init() {
-    even = fetch(0);
-    odd = fetch(1);
+    const int a = fetch(g0), b = fetch(g0 + 1);
+    even = (g0 & 1) ? b : a;
+    odd = (g0 & 1) ? a : b;
   }
   // Call before tile j's V load (the K loads run ahead, in tile j / 4 or
   // later): group j / 4 - 1 is dead, so group j / 4 + 1 takes its register.
   __device__ __forceinline__ void advance(int j) {
-    if (j < 4 || (j & 3) != 0) return;
+    if ((j & 3) != 0 || (j >> 2) <= g0) return;
     const int g = j / 4 + 1;
     if (g & 1)
       odd = fetch(g);
@@ -920,22 +922,205 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 // of G, so a CTA that drew a long unit in one round draws a short one in the
 // next. Each CTA decodes its whole list once, before it starts.
 constexpr int kTcMaxUnitsPerCta = 64;
-constexpr int kTcPersistSmem = TcLayout<false>::kSmemBytes + 256;  // + the unit list
+constexpr int kTcUnitInts = 4;  // per list entry: item id, record base, ticket, parts
+constexpr int kTcPersistSmem =
+    TcLayout<false>::kSmemBytes + kTcMaxUnitsPerCta * kTcUnitInts * 4;  // + the unit list
+// Split-KV: a unit of more than twice the launch's average work per SM is cut
+// into at most kTcMaxParts KV parts of at least kTcMinPartTiles tiles each
+// (a unit only a little above the average gains less than its merge costs).
+constexpr int kTcMaxParts = 8;
+constexpr int kTcMinPartTiles = 4;
+// A part record per Q tile is column-major, [130][128 rows]: O columns 0-127,
+// then m, then l, so a warp's rows are consecutive floats (coalesced).
+constexpr int kTcRecordFloats = 130 * kTcRows;
 
 __device__ __forceinline__ int tc_snake_pos(int k, int cta, int grid) {
   return k * grid + ((k & 1) ? grid - 1 - cta : cta);
 }
 
+// KV parts of a unit of `cost` tiles under the split target (0: no split).
+__device__ __forceinline__ int tc_parts(int cost, int target) {
+  if (target <= 0 || cost <= 2 * target) return 1;
+  return min(kTcMaxParts, (cost + target - 1) / target);
+}
+
+__device__ __forceinline__ int tc_cached_cost(const PrefillParams& p, const int* cost, int id) {
+  return id < kTcCachedPairs ? cost[id] : tc_unit_cost(p, id / p.blocks_per_seq, id % p.blocks_per_seq);
+}
+
+// The launch's split target, the same in every CTA: the average work per SM
+// (every unit's KV tiles / SMs, at least kTcMinPartTiles), raised until the
+// split units' parts fit the workspace's records; 0 without a workspace.
+// Then the histogram of item cost keys: a unit of cost c in P parts is P
+// items of key ceil(c / P); the number of items is left in scratch int
+// kTcHistInts + 3. Call with all threads of the CTA; `scratch` as for
+// tc_build_hist (its 4 result ints serve as reduction slots).
+__device__ __forceinline__ int tc_build_split_hist(const PrefillParams& p, int* scratch) {
+  int* hist = scratch;
+  int* red = scratch + kTcHistInts;  // [0] total tiles, [1] split parts, [2] target
+  int* cost = scratch + kTcHistInts + 4;
+  const int pairs = p.num_seqs * p.blocks_per_seq;
+  for (int i = threadIdx.x; i < kTcHistInts / 4; i += blockDim.x)
+    reinterpret_cast<int4*>(hist)[i] = make_int4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    red[0] = 0;
+    red[3] = 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int c = tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq);
+    if (i < kTcCachedPairs) cost[i] = c;
+    atomicAdd(&red[0], c);
+  }
+  __syncthreads();
+  int target = 0;
+  if (p.split_cap > 0 && p.num_sms > 0) {
+    const int64_t total = (int64_t)red[0] * p.num_kv_heads;
+    const int64_t avg = (total + p.num_sms - 1) / p.num_sms;
+    target = avg > kTcMinPartTiles ? (int)avg : kTcMinPartTiles;
+    for (int round = 0; round < 64; ++round) {
+      __syncthreads();
+      if (threadIdx.x == 0) red[1] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+        const int parts = tc_parts(tc_cached_cost(p, cost, i), target);
+        if (parts > 1) atomicAdd(&red[1], parts);
+      }
+      __syncthreads();
+      if ((int64_t)red[1] * p.num_kv_heads <= p.split_cap) break;
+      target += target / 4 + 1;
+    }
+    if ((int64_t)red[1] * p.num_kv_heads > p.split_cap) target = 0;  // never split then
+  }
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int c = tc_cached_cost(p, cost, i);
+    const int parts = tc_parts(c, target);
+    atomicAdd(&hist[tc_hist_slot((c + parts - 1) / parts)], parts);
+    atomicAdd(&red[3], parts);  // items
+  }
+  __syncthreads();
+  return target;
+}
+
+// The item (pair, part) at position `item_pos` of the longest-first item
+// order (ties by pair id, then part), from tc_build_split_hist's histogram.
+// Warp-collective; the result is the same in every lane.
+__device__ __forceinline__ void tc_item_at(const PrefillParams& p, const int* scratch, int target,
+                                           int item_pos, int lane, int& pair, int& part) {
+  const int* hist = scratch;
+  const int* cost = scratch + kTcHistInts + 4;
+  const int pairs = p.num_seqs * p.blocks_per_seq;
+  const unsigned full = 0xffffffffu;
+  constexpr int kPerLane = kTcCostKeys / 32;
+  const int chunk_lo = kTcCostKeys - kPerLane * (lane + 1);
+  int chunk = 0;
+#pragma unroll
+  for (int k = 0; k < kPerLane / 4; ++k) {
+    const int4 h = reinterpret_cast<const int4*>(hist + tc_hist_slot(chunk_lo))[k];
+    chunk += (h.x + h.y) + (h.z + h.w);
+  }
+  int incl = chunk;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(full, incl, d);
+    if (lane >= d) incl += v;
+  }
+  const unsigned own = __ballot_sync(full, item_pos >= incl - chunk && item_pos < incl);
+  const int o = own ? __ffs(own) - 1 : 0;
+  const int before_o = __shfl_sync(full, incl - chunk, o);
+  const int hi = kTcCostKeys - 1 - kPerLane * o - 2 * lane;
+  const int h0 = hist[tc_hist_slot(hi)], h1 = hist[tc_hist_slot(hi - 1)];
+  int incl2 = h0 + h1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(full, incl2, d);
+    if (lane >= d) incl2 += v;
+  }
+  const int first = before_o + incl2 - (h0 + h1);
+  int key = -1, rank = 0;
+  if (item_pos >= first && item_pos < first + h0) {
+    key = hi;
+    rank = item_pos - first;
+  } else if (item_pos >= first + h0 && item_pos < first + h0 + h1) {
+    key = hi - 1;
+    rank = item_pos - first - h0;
+  }
+  const unsigned owner = __ballot_sync(full, key >= 0);
+  const int src = owner ? __ffs(owner) - 1 : 0;
+  key = __shfl_sync(full, key, src);
+  rank = __shfl_sync(full, rank, src);
+  // the rank-th item of key `key`: pairs in id order, each with its parts
+  pair = 0;
+  part = 0;
+  for (int base = 0; base < pairs; base += 32) {
+    const int id = base + lane;
+    int w = 0;
+    if (id < pairs) {
+      const int c = tc_cached_cost(p, cost, id);
+      const int parts = tc_parts(c, target);
+      w = (c + parts - 1) / parts == key ? parts : 0;
+    }
+    int wincl = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(full, wincl, d);
+      if (lane >= d) wincl += v;
+    }
+    const int chunk_items = __shfl_sync(full, wincl, 31);
+    if (rank < chunk_items) {
+      const unsigned hit = __ballot_sync(full, wincl > rank);
+      const int l = __ffs(hit) - 1;
+      pair = base + l;
+      part = rank - (__shfl_sync(full, wincl, l) - __shfl_sync(full, w, l));
+      break;
+    }
+    rank -= chunk_items;
+  }
+}
+
+// For a split pair: (split pairs, their parts) before it in id order.
+// Warp-collective.
+__device__ __forceinline__ void tc_split_prefix(const PrefillParams& p, const int* scratch,
+                                                int target, int pair, int lane, int& n_before,
+                                                int& parts_before) {
+  const int* cost = scratch + kTcHistInts + 4;
+  n_before = 0;
+  parts_before = 0;
+  for (int base = 0; base < pair; base += 32) {
+    const int id = base + lane;
+    int parts = 1;
+    if (id < pair) parts = tc_parts(tc_cached_cost(p, cost, id), target);
+    int a = (id < pair && parts > 1) ? 1 : 0;
+    int b = a ? parts : 0;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, d);
+      b += __shfl_xor_sync(0xffffffffu, b, d);
+    }
+    n_before += a;
+    parts_before += b;
+  }
+}
+
 struct TcUnit {
   int s, kvh, q_start, q_len, seq_len, ctx, tok_begin, n_a, n_b, n_total;
+  // KV part: tiles [lo, lo + n) of the unit's n_total; parts == 1 unless split
+  int part, parts, lo, n, rec, ticket;
 };
 
-// Everything a role needs about unit `id` (= pair * num_kv_heads + KV head);
-// n_total = 0 for a row block past the sequence's chunk.
-__device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, int id) {
+// Everything a role needs about list entry `e` (item id = (pair *
+// num_kv_heads + KV head) * kTcMaxParts + part, record base, ticket, parts);
+// n = 0 for a row block past the sequence's chunk.
+__device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, const int* e) {
   TcUnit u;
-  const int pair = id / p.num_kv_heads;
-  u.kvh = id - pair * p.num_kv_heads;
+  const int id = e[0];
+  u.part = id % kTcMaxParts;
+  const int unit = id / kTcMaxParts;
+  const int pair = unit / p.num_kv_heads;
+  u.kvh = unit - pair * p.num_kv_heads;
+  u.rec = e[1];
+  u.ticket = e[2];
+  u.parts = e[3];
   u.s = pair / p.blocks_per_seq;
   const int rb = pair - u.s * p.blocks_per_seq;
   u.q_start = __ldg(p.query_start_loc + u.s);
@@ -945,6 +1130,7 @@ __device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, int id) {
   const int tpc = (kTcTiles * kTcRows) / p.group;
   u.tok_begin = rb * tpc;
   u.n_a = u.n_b = u.n_total = 0;
+  u.lo = u.n = 0;
   if (u.tok_begin >= u.q_len || u.seq_len <= 0) return u;
   int n[kTcTiles];
 #pragma unroll
@@ -957,9 +1143,15 @@ __device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, int id) {
     const int kv_limit = min(u.seq_len, max(1, u.ctx + last_tok + 1));
     n[x] = (kv_limit + kTcKv - 1) / kTcKv;
   }
-  u.n_a = n[0];
-  u.n_b = n[1];
   u.n_total = max(n[0], n[1]);
+  // part `part` of `parts`: tiles [part * n / parts, (part + 1) * n / parts),
+  // never empty because parts <= n
+  u.lo = u.part * u.n_total / u.parts;
+  const int hi = (u.part + 1) * u.n_total / u.parts;
+  u.n = hi - u.lo;
+  // this part's tiles of each Q tile (a Q tile with fewer tiles may have none)
+  u.n_a = max(0, min(hi, n[0]) - u.lo);
+  u.n_b = max(0, min(hi, n[1]) - u.lo);
   return u;
 }
 
@@ -990,22 +1182,36 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
   uint64_t* q_empty = bars + 21;    // a unit's last S MMAs retired -> producer (next Q)
   uint64_t* o_free = bars + 22;     // [2] per Q tile: epilogue read O (128 arrivals) -> MMA
   uint64_t* pv0_done = bars + 24;   // [2] per Q tile: a tile's first-half PV MMAs retired
-  int* units = reinterpret_cast<int*>(bars + 32);  // [kTcMaxUnitsPerCta] unit ids
+  uint64_t* merge_bar = bars + 26;  // [2] per Q tile: split records written / ticket known
+  int* merge_ticket = reinterpret_cast<int*>(bars + 28);  // [2] per Q tile
+  int* units = reinterpret_cast<int*>(bars + 32);  // [kTcMaxUnitsPerCta][kTcUnitInts]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total = p.num_seqs * p.blocks_per_seq * p.num_kv_heads;
-  int n_units = 0;
-  while (n_units < kTcMaxUnitsPerCta && tc_snake_pos(n_units, blockIdx.x, gridDim.x) < total)
-    ++n_units;
 
   // ---- this CTA's unit list, from the longest-first order (Q region as scratch) ----
   int* scratch = reinterpret_cast<int*>(smem + kTcQ);
-  tc_build_hist(p, scratch);
+  const int target = tc_build_split_hist(p, scratch);
+  const int total = scratch[kTcHistInts + 3] * p.num_kv_heads;  // items x KV heads
+  int n_units = 0;
+  while (n_units < kTcMaxUnitsPerCta && tc_snake_pos(n_units, blockIdx.x, gridDim.x) < total)
+    ++n_units;
   for (int k = warp; k < n_units; k += blockDim.x / 32) {
     const int pos = tc_snake_pos(k, blockIdx.x, gridDim.x);
-    const int pair = tc_pair_at(p, scratch, pos / p.num_kv_heads, lane);
-    if (lane == 0) units[k] = pair * p.num_kv_heads + pos % p.num_kv_heads;
+    const int kvh = pos % p.num_kv_heads;
+    int pair, part;
+    tc_item_at(p, scratch, target, pos / p.num_kv_heads, lane, pair, part);
+    const int parts =
+        tc_parts(tc_cached_cost(p, scratch + kTcHistInts + 4, pair), target);
+    int n_before = 0, parts_before = 0;
+    if (parts > 1) tc_split_prefix(p, scratch, target, pair, lane, n_before, parts_before);
+    if (lane == 0) {
+      int* e = units + k * kTcUnitInts;
+      e[0] = (pair * p.num_kv_heads + kvh) * kTcMaxParts + part;
+      e[1] = parts_before * p.num_kv_heads + kvh * parts;  // first record of the unit
+      e[2] = n_before * p.num_kv_heads + kvh;              // its ticket
+      e[3] = parts;
+    }
   }
 
   const uint32_t sbase = smem_u32(smem);
@@ -1025,6 +1231,7 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
       mbar_init(smem_u32(&o_done[x]), 1);
       mbar_init(smem_u32(&o_free[x]), kTcRows);
       mbar_init(smem_u32(&pv0_done[x]), 1);
+      mbar_init(smem_u32(&merge_bar[x]), kTcRows);
     }
     mbar_init(smem_u32(mma_drain), 1);
     mbar_init(smem_u32(q_full), 1);
@@ -1051,14 +1258,16 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
     int issued_k = 0, issued_v = 0, units_q = 0;
     int gk = 0, gv = 0;  // first global K / V tile index of the current unit
     for (int k = 0; k < n_units && ok; ++k) {
-      const TcUnit U = tc_unit(p, units[k]);
-      if (U.n_total == 0) continue;
+      const TcUnit U = tc_unit(p, units + k * kTcUnitInts);
+      if (U.n == 0) continue;
       const int max_page_idx = (U.seq_len - 1) / p.block_size;
       TilePages pages{p.block_tables + (int64_t)U.s * p.block_table_stride, max_page_idx,
-                      p.block_size, lane, 0, 0};
+                      p.block_size, lane, 0, 0, U.lo >> 2};
       pages.init();
-      auto load = [&](bool is_v, int j) -> bool {
-        const int g = (is_v ? gv : gk) + j;
+      // jj: tile of this part (0 .. n - 1); the unit's tile is U.lo + jj
+      auto load = [&](bool is_v, int jj) -> bool {
+        const int g = (is_v ? gv : gk) + jj;
+        const int j = U.lo + jj;
         const int nst = is_v ? kTcVStages : kKSt;
         const int st = g % nst;
         uint64_t* empty = is_v ? v_empty : k_empty;
@@ -1106,12 +1315,12 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
       }
       __syncwarp();
       ++units_q;
-      const int n = U.n_total;
-      for (int j = 0; j < min(2, n) && ok; ++j) ok = load(false, j);
-      for (int j = 0; j < n && ok; ++j) {
-        pages.advance(j);
-        ok = load(true, j);
-        if (ok && j + 2 < n) ok = load(false, j + 2);
+      const int n = U.n;
+      for (int jj = 0; jj < min(2, n) && ok; ++jj) ok = load(false, jj);
+      for (int jj = 0; jj < n && ok; ++jj) {
+        pages.advance(U.lo + jj);
+        ok = load(true, jj);
+        if (ok && jj + 2 < n) ok = load(false, jj + 2);
       }
       gk += n;
       gv += n;
@@ -1183,10 +1392,10 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
       int ts[kTcTiles] = {0, 0};  // tile steps per Q tile (s_full / p_ready phases)
       int ep[kTcTiles] = {0, 0};  // units with rows per Q tile (o_done / o_free phases)
       for (int k = 0; k < n_units && ok; ++k) {
-        const TcUnit U = tc_unit(p, units[k]);
-        if (U.n_total == 0) continue;
-        const int nx[kTcTiles] = {U.n_a, U.n_b};
-        const int n = U.n_total;
+        const TcUnit U = tc_unit(p, units + k * kTcUnitInts);
+        if (U.n == 0) continue;
+        const int nx[kTcTiles] = {U.n_a, U.n_b};  // this part's tiles per Q tile
+        const int n = U.n;
         // S of tile 0 for both Q tiles, once this unit's Q landed
         if (!mbar_wait(smem_u32(q_full), units_q & 1) || !wait_k(gk)) {
           ok = false;
@@ -1262,12 +1471,14 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
     const float scale = p.scale_log2;
     const int group = p.group;
     const int tpc = (kTcTiles * kTcRows) / group;
-    int ts = 0, ep = 0, gv = 0;
+    int ts = 0, ep = 0, gv = 0, mp = 0;
     for (int k = 0; k < n_units && ok; ++k) {
-      const TcUnit U = tc_unit(p, units[k]);
-      const int my_tiles = x_tile ? U.n_b : U.n_a;
-      if (my_tiles == 0) {
-        gv += U.n_total;
+      const TcUnit U = tc_unit(p, units + k * kTcUnitInts);
+      const int my_tiles = x_tile ? U.n_b : U.n_a;  // this part's tiles of this Q tile
+      // a Q tile with no tiles in a part of a split unit still hands in an
+      // (empty) record and takes its ticket
+      if (my_tiles == 0 && U.parts == 1) {
+        gv += U.n;
         continue;
       }
       const int seq_len = U.seq_len;
@@ -1336,7 +1547,7 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
           break;
         }
         tc_fence_after_sync();
-        const int kbase = j * kTcKv;
+        const int kbase = (U.lo + j) * kTcKv;  // j counts this part's tiles
         // columns [0, lim) of this tile are visible to this row
         const int lim = min(qpos - kbase + 1, seq_len - kbase);
         const bool need_mask = lim < kTcKv;
@@ -1455,6 +1666,115 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
         ++ts;
       }
       if (!ok) break;
+      if (U.parts > 1) {
+        // ---- split unit: this part's record (O, m, l per row); the part
+        // that takes the last ticket merges every part into the output ----
+        const int64_t part_floats = (int64_t)kTcTiles * kTcRecordFloats;
+        float* rec0 = p.split_records + (int64_t)U.rec * part_floats +
+                      (int64_t)x_tile * kTcRecordFloats + t;  // this row of part 0
+        float* rec = rec0 + (int64_t)U.part * part_floats;
+        if (my_tiles > 0) {
+          const bool done = mbar_wait(smem_u32(&o_done[x_tile]), ep & 1);
+          if (!__all_sync(0xffffffffu, done)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t ob[2][32];
+            tmem_ld32_issue(tO + h * 64, ob[0]);
+            tmem_ld32_issue(tO + h * 64 + 32, ob[1]);
+            tmem_wait_ld32(ob[0]);
+            tmem_wait_ld32(ob[1]);
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                rec[(h * 64 + c * 32 + i) * kTcRows] = __uint_as_float(ob[c][i]);
+          }
+          tc_fence_before_sync();
+          mbar_arrive(smem_u32(&o_free[x_tile]));
+          ++ep;
+        }
+        rec[128 * kTcRows] = my_tiles > 0 ? m_used : kNegInf;
+        rec[129 * kTcRows] = my_tiles > 0 ? l : 0.f;
+        __threadfence();  // the record is visible before the ticket is taken
+        mbar_arrive(smem_u32(&merge_bar[x_tile]));
+        bool got = mbar_wait(smem_u32(&merge_bar[x_tile]), mp & 1);
+        ++mp;
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (t == 0)
+          merge_ticket[x_tile] = atomicAdd(p.split_tickets + U.ticket * kTcTiles + x_tile, 1);
+        mbar_arrive(smem_u32(&merge_bar[x_tile]));
+        got = mbar_wait(smem_u32(&merge_bar[x_tile]), mp & 1);
+        ++mp;
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        // the last part puts the ticket back to 0: a launch leaves its tickets
+        // as it found them (zero), so none is cleared before a launch
+        if (t == 0 && merge_ticket[x_tile] == U.parts - 1)
+          p.split_tickets[U.ticket * kTcTiles + x_tile] = 0;
+        if (merge_ticket[x_tile] == U.parts - 1 && row_token >= 0) {
+          __threadfence();  // every other part's record, seen through L2
+          // Every load below is issued for all parts at once (parts past
+          // U.parts read part 0 and get weight 0), so the merge costs a few
+          // L2 round trips instead of one per part and column chunk.
+          float w[kTcMaxParts], lq[kTcMaxParts];
+#pragma unroll
+          for (int q = 0; q < kTcMaxParts; ++q) {
+            const float* src = rec0 + (q < U.parts ? q : 0) * part_floats;
+            w[q] = __ldcg(src + 128 * kTcRows);
+            lq[q] = __ldcg(src + 129 * kTcRows);
+          }
+          float m = kNegInf;
+#pragma unroll
+          for (int q = 0; q < kTcMaxParts; ++q)
+            if (q < U.parts) m = fmaxf(m, w[q]);
+          float lsum = 0.f;
+#pragma unroll
+          for (int q = 0; q < kTcMaxParts; ++q) {
+            // a part that saw no key of the row (m = -inf), or no part, weighs 0
+            w[q] = (q < U.parts && w[q] != kNegInf) ? fast_exp2(w[q] - m) : 0.f;
+            lsum += w[q] > 0.f ? w[q] * lq[q] : 0.f;
+          }
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+          uint4* orow = reinterpret_cast<uint4*>(
+              reinterpret_cast<T*>(p.out) + (int64_t)(U.q_start + row_token) * p.out_token_stride +
+              (int64_t)row_head * p.out_head_stride);
+#pragma unroll 1
+          for (int c8 = 0; c8 < kHeadDim / 8; ++c8) {
+            float v[kTcMaxParts][8];
+#pragma unroll
+            for (int q = 0; q < kTcMaxParts; ++q) {
+              const float* src = rec0 + (q < U.parts ? q : 0) * part_floats + c8 * 8 * kTcRows;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[q][i] = __ldcg(src + i * kTcRows);
+            }
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc[i] = 0.f;
+#pragma unroll
+              for (int q = 0; q < kTcMaxParts; ++q)
+                acc[i] += w[q] > 0.f ? w[q] * v[q][i] : 0.f;  // never 0 * garbage
+            }
+            uint4 pk;
+            pk.x = pack2<T>(acc[0] * inv, acc[1] * inv);
+            pk.y = pack2<T>(acc[2] * inv, acc[3] * inv);
+            pk.z = pack2<T>(acc[4] * inv, acc[5] * inv);
+            pk.w = pack2<T>(acc[6] * inv, acc[7] * inv);
+            orow[c8] = pk;
+          }
+        }
+        gv += U.n;
+        continue;
+      }
       // ---- epilogue: O / l to the output rows, then O_X is free ----
       const bool done = mbar_wait(smem_u32(&o_done[x_tile]), ep & 1);
       if (!__all_sync(0xffffffffu, done)) {
@@ -1498,7 +1818,7 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
         for (int i = 0; i < 16; ++i) orow[i] = packed[i];
       }
       ++ep;
-      gv += U.n_total;
+      gv += U.n;
     }
     if (!ok && lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
   }
@@ -1539,8 +1859,11 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
       if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
       if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
         return e;
-      int64_t grid = units < sms ? units : sms;
-      const int64_t min_grid = (units + kTcMaxUnitsPerCta - 1) / kTcMaxUnitsPerCta;
+      q.num_sms = sms;
+      // split parts add at most split_cap items to the units
+      const int64_t items = units + (q.split_cap > 0 ? q.split_cap : 0);
+      int64_t grid = items < sms ? items : sms;
+      const int64_t min_grid = (items + kTcMaxUnitsPerCta - 1) / kTcMaxUnitsPerCta;
       if (grid < min_grid) grid = min_grid;
       pkernel<<<(unsigned)grid, tc_threads<false>(), kTcPersistSmem, stream>>>(mk, mv, mq, q);
       return cudaGetLastError();

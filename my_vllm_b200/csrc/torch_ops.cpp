@@ -209,7 +209,8 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
                    double softmax_scale, int64_t num_seqs,
                    const std::optional<at::Tensor>& k_scale,
                    const std::optional<at::Tensor>& v_scale,
-                   const std::optional<at::Tensor>& status) {
+                   const std::optional<at::Tensor>& status,
+                   const std::optional<at::Tensor>& workspace) {
   require_cuda(q, "q");
   require_cuda(out, "out");
   TORCH_CHECK(q.dim() == 3 && out.sizes() == q.sizes() && q.stride(2) == 1 && out.stride(2) == 1,
@@ -222,13 +223,20 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
                   block_tables.size(0) >= num_seqs && seq_lens.numel() >= num_seqs,
               "b200: query_start_loc / block_tables / seq_lens too short for num_seqs");
   const b200_paged_cache cache = cache_desc(k_cache, v_cache, q.scalar_type(), k_scale, v_scale);
+  void* ws = nullptr;
+  int64_t ws_bytes = 0;
+  if (workspace.has_value()) {
+    require_cuda(*workspace, "workspace");
+    ws = workspace->data_ptr();
+    ws_bytes = workspace->numel() * workspace->element_size();
+  }
   check_abi(b200_paged_prefill(q.data_ptr(), q.stride(0), q.stride(1), &cache,
                                block_tables.data_ptr<int32_t>(), block_tables.stride(0),
                                seq_lens.data_ptr<int32_t>(), query_start_loc.data_ptr<int32_t>(),
                                static_cast<int32_t>(num_seqs), static_cast<int32_t>(q.size(0)),
                                static_cast<int32_t>(max_q_len),
                                static_cast<int32_t>(q.size(1)), out.data_ptr(), out.stride(0),
-                               out.stride(1), static_cast<float>(softmax_scale),
+                               out.stride(1), static_cast<float>(softmax_scale), ws, ws_bytes,
                                status_ptr(status), current_stream(q)),
             "b200_paged_prefill");
 }
@@ -247,7 +255,8 @@ void paged_decode_meta(const at::Tensor&, const at::Tensor&, const at::Tensor&,
 void paged_prefill_meta(const at::Tensor&, const at::Tensor&, const at::Tensor&,
                         const at::Tensor&, const at::Tensor&, const at::Tensor&, at::Tensor&,
                         int64_t, double, int64_t, const std::optional<at::Tensor>&,
-                        const std::optional<at::Tensor>&, const std::optional<at::Tensor>&) {}
+                        const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                        const std::optional<at::Tensor>&) {}
 
 }  // namespace
 
@@ -265,7 +274,7 @@ TORCH_LIBRARY(b200, m) {
       "paged_prefill(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
       "Tensor seq_lens, Tensor query_start_loc, Tensor(a!) out, int max_q_len, "
       "float softmax_scale, int num_seqs, Tensor? k_scale=None, Tensor? v_scale=None, "
-      "Tensor(b!)? status=None) -> ()");
+      "Tensor(b!)? status=None, Tensor(c!)? workspace=None) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {

@@ -527,8 +527,13 @@ def paged_prefill(
     k_scale: torch.Tensor | None = None,
     v_scale: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Causal paged prefill over ``num_seqs`` sequences into ``out`` (in place)."""
+    """Causal paged prefill over ``num_seqs`` sequences into ``out`` (in place).
+    ``workspace`` (``prefill_workspace_bytes()`` of device memory, optional,
+    zeroed before its first use and again after a launch that reported an
+    error) lets units much longer than the batch's average work per SM be
+    split over several CTAs; launches sharing a workspace must not overlap."""
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
                     ("block_tables", block_tables), ("seq_lens", seq_lens),
                     ("query_start_loc", query_start_loc), ("out", out)):
@@ -547,6 +552,15 @@ def paged_prefill(
     if query_start_loc.numel() < S + 1 or block_tables.size(0) < S:
         raise ValueError("query_start_loc / block_tables too short for num_seqs")
     paged_cache_desc(k_cache, v_cache, q.dtype, k_scale, v_scale)  # cached layout checks
+    if workspace is not None and workspace.numel() * workspace.element_size() < prefill_workspace_bytes():
+        raise ValueError("prefill workspace smaller than prefill_workspace_bytes()")
     _ops().paged_prefill(q, k_cache, v_cache, block_tables, seq_lens, query_start_loc, out,
-                         int(max_q_len), float(softmax_scale), S, k_scale, v_scale, status)
+                         int(max_q_len), float(softmax_scale), S, k_scale, v_scale, status,
+                         workspace)
     return out
+
+
+@functools.lru_cache(maxsize=1)
+def prefill_workspace_bytes() -> int:
+    """Bytes of the optional prefill workspace (split-KV partial results)."""
+    return int(_native.load_library().b200_paged_prefill_workspace_bytes())

@@ -90,8 +90,18 @@ def test_prefill_and_append_reject_unsupported_shapes():
     cache = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 64, _native.DTYPE_BFLOAT16,
                                16 * 8 * 64, 8 * 64, 64)
     rc = lib.b200_paged_prefill(0x3000, 32 * 64, 64, cache, 0x4000, 2, 0x5000, 0x6000, 2, 10,
-                                5, 32, 0x7000, 32 * 64, 64, 0.125, None, None)
+                                5, 32, 0x7000, 32 * 64, 64, 0.125, None, 0, None, None)
     assert rc == _native.B200_ERR_UNSUPPORTED
+    # the optional split-KV workspace: a size query, and too small a workspace is refused
+    need = lib.b200_paged_prefill_workspace_bytes()
+    assert need > 0 and need % 256 == 0
+    cache128 = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_BFLOAT16,
+                                  16 * 8 * 128, 8 * 128, 128)
+    rc = lib.b200_paged_prefill(0x3000, 32 * 128, 128, cache128, 0x4000, 2, 0x5000, 0x6000, 2,
+                                10, 5, 32, 0x7000, 32 * 128, 128, 0.088, 0x8000, need - 256,
+                                None, None)
+    assert rc == _native.B200_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.b200_last_error()
     rc = lib.b200_store_kvcache(0x1000, 1024, 0x2000, 1024, 0x3000, 0x4000, 1024, 0x5000, 0,
                                 4, 1024, 1, 64, None, None)
     assert rc == _native.B200_ERR_UNSUPPORTED  # 1-byte elements
@@ -122,7 +132,7 @@ def test_fp8_cache_arguments_checked_before_launch():
     fp8 = _native.PagedCache(0x1000, 0x2000, 16, 16, 8, 128, _native.DTYPE_FP8_E4M3,
                              16 * 8 * 128, 8 * 128, 128, 1, None, None)
     rc = lib.b200_paged_prefill(0x3000, 32 * 128, 128, fp8, 0x4000, 2, 0x5000, 0x6000, 2, 10,
-                                5, 32, 0x7000, 32 * 128, 128, 0.088, None, None)
+                                5, 32, 0x7000, 32 * 128, 128, 0.088, None, 0, None, None)
     assert rc == _native.B200_ERR_UNSUPPORTED
     # the FP8 append wants rows of whole 16-byte vectors
     rc = lib.b200_store_kvcache_fp8(0x1000, 1024, 0x2000, 1024, _native.DTYPE_BFLOAT16, 0x3000,
