@@ -605,7 +605,7 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   CUtensorMap mk, mv;
   if ((rc = cache_tensor_map(cache->k_cache, *cache, &mk)) != B200_OK) return rc;
   if ((rc = cache_tensor_map(cache->v_cache, *cache, &mv)) != B200_OK) return rc;
-  b200::PrefillParams p;
+  b200::PrefillParams p{};
   p.q = q;
   p.q_token_stride = q_token_stride;
   p.q_head_stride = q_head_stride;
@@ -616,6 +616,8 @@ int b200_paged_prefill(const void* q, int64_t q_token_stride, int64_t q_head_str
   p.out = out;
   p.out_token_stride = out_token_stride;
   p.out_head_stride = out_head_stride;
+  p.out_v8 = (reinterpret_cast<uintptr_t>(out) % 32 == 0 &&
+              ((out_token_stride | out_head_stride) & 15) == 0) ? 1 : 0;
   p.block_size = cache->block_size;
   p.group = group;
   p.num_q_heads = num_q_heads;

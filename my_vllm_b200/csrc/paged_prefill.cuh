@@ -32,6 +32,8 @@ struct PrefillParams {
                        // 128); 0: the softmax warps stage it
   int o_tma;           // 1: Q tiles whose rows all belong to the sequence leave by a
                        // TMA store through the out tensor map; 0: per-thread stores
+  int out_v8;          // 1: out is 32-byte aligned with strides that are multiples of
+                       // 16 elements (rows leave in 32-byte stores)
   int32_t* status;
   // Split-KV (persistent kernel, 16-bit caches): a unit costlier than the
   // average per-SM work is cut into KV parts on different CTAs; the part

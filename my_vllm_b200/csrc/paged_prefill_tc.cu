@@ -120,9 +120,8 @@ __device__ __forceinline__ uint32_t pair_to_f16(uint32_t w, __nv_bfloat16) {
 // position's rank inside that bucket in id order.
 constexpr int kTcCostKeys = 2048;  // cost keys are clamped here: order only, never results
 
-__device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int rb) {
-  const int q_len = __ldg(p.query_start_loc + s + 1) - __ldg(p.query_start_loc + s);
-  const int seq_len = __ldg(p.seq_lens + s);
+// Cost of row block rb of a sequence with q_len new tokens and seq_len keys.
+__device__ __forceinline__ int tc_cost_of(const PrefillParams& p, int q_len, int seq_len, int rb) {
   const int tpc = (kTcTiles * kTcRows) / p.group;
   const int tok_begin = rb * tpc;
   if (tok_begin >= q_len || seq_len <= 0) return 0;
@@ -132,6 +131,11 @@ __device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int r
   return min((kv_limit + kTcKv - 1) / kTcKv, kTcCostKeys - 1);
 }
 
+__device__ __forceinline__ int tc_unit_cost(const PrefillParams& p, int s, int rb) {
+  const int q_len = __ldg(p.query_start_loc + s + 1) - __ldg(p.query_start_loc + s);
+  return tc_cost_of(p, q_len, __ldg(p.seq_lens + s), rb);
+}
+
 // Pair costs kept in shared memory by tc_decode_unit (beyond this many pairs
 // the rank search recomputes them from the metadata).
 constexpr int kTcCachedPairs = 8192;
@@ -139,7 +143,10 @@ constexpr int kTcCachedPairs = 8192;
 // each sum one 64-key chunk with 16-byte loads spread over the banks.
 constexpr int kTcHistInts = kTcCostKeys + kTcCostKeys / 16;
 __device__ __forceinline__ int tc_hist_slot(int key) { return key + (key >> 6) * 4; }
-constexpr int kTcScratchInts = kTcHistInts + 4 + kTcCachedPairs;
+// The persistent kernel also keeps (first query row, new tokens, keys) of the
+// first kTcSeqCache sequences in its scratch, after the pair costs.
+constexpr int kTcSeqCache = 1024;
+constexpr int kTcScratchInts = kTcHistInts + 4 + kTcCachedPairs + 3 * kTcSeqCache;
 static_assert(kTcScratchInts * 4 <= kTcTiles * 2 * kTcHalf, "scratch lives in the Q tiles");
 
 // Histogram of the (sequence, row block) pair costs, plus a cache of the
@@ -271,10 +278,16 @@ struct TilePages {
     const int tok = (g * 4 + (lane >> 3)) * kTcKv + (lane & 7) * kTileTokens;
     return __ldg(bt_row + min(tok / block_size, max_page_idx));
   }
+  // g0 is warp-uniform: a branch, not a select, so no instruction waits on
+  // the loads until a page id is used
   __device__ __forceinline__ void init() {
-    const int a = fetch(g0), b = fetch(g0 + 1);
-    even = (g0 & 1) ? b : a;
-    odd = (g0 & 1) ? a : b;
+    if (g0 & 1) {
+      odd = fetch(g0);
+      even = fetch(g0 + 1);
+    } else {
+      even = fetch(g0);
+      odd = fetch(g0 + 1);
+    }
   }
   // Call before tile j's V load (the K loads run ahead, in tile j / 4 or
   // later): group j / 4 - 1 is dead, so group j / 4 + 1 takes its register.
@@ -922,9 +935,14 @@ __global__ void __launch_bounds__(tc_threads<kFp8>(), 1)
 // of G, so a CTA that drew a long unit in one round draws a short one in the
 // next. Each CTA decodes its whole list once, before it starts.
 constexpr int kTcMaxUnitsPerCta = 64;
-constexpr int kTcUnitInts = 4;  // per list entry: item id, record base, ticket, parts
+// per list entry: item id, record base, ticket | parts << 24, and the
+// sequence's first query row, new tokens and keys (read at set-up, so that no
+// role waits on a global load when it moves to its next unit: under the
+// streaming of every SM one such round trip took microseconds)
+constexpr int kTcUnitInts = 6;
 constexpr int kTcPersistSmem =
     TcLayout<false>::kSmemBytes + kTcMaxUnitsPerCta * kTcUnitInts * 4;  // + the unit list
+static_assert(kTcPersistSmem <= 227 * 1024, "shared memory budget");
 // Split-KV: a unit of more than twice the launch's average work per SM is cut
 // into at most kTcMaxParts KV parts of at least kTcMinPartTiles tiles each
 // (a unit only a little above the average gains less than its merge costs).
@@ -959,7 +977,14 @@ __device__ __forceinline__ int tc_build_split_hist(const PrefillParams& p, int* 
   int* hist = scratch;
   int* red = scratch + kTcHistInts;  // [0] total tiles, [1] split parts, [2] target
   int* cost = scratch + kTcHistInts + 4;
+  int* seqc = cost + kTcCachedPairs;  // [kTcSeqCache][3]
   const int pairs = p.num_seqs * p.blocks_per_seq;
+  for (int s = threadIdx.x; s < min(p.num_seqs, kTcSeqCache); s += blockDim.x) {
+    const int q0 = __ldg(p.query_start_loc + s);
+    seqc[3 * s] = q0;
+    seqc[3 * s + 1] = __ldg(p.query_start_loc + s + 1) - q0;
+    seqc[3 * s + 2] = __ldg(p.seq_lens + s);
+  }
   for (int i = threadIdx.x; i < kTcHistInts / 4; i += blockDim.x)
     reinterpret_cast<int4*>(hist)[i] = make_int4(0, 0, 0, 0);
   if (threadIdx.x == 0) {
@@ -968,7 +993,9 @@ __device__ __forceinline__ int tc_build_split_hist(const PrefillParams& p, int* 
   }
   __syncthreads();
   for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
-    const int c = tc_unit_cost(p, i / p.blocks_per_seq, i % p.blocks_per_seq);
+    const int s = i / p.blocks_per_seq;
+    const int c = s < kTcSeqCache ? tc_cost_of(p, seqc[3 * s + 1], seqc[3 * s + 2], i % p.blocks_per_seq)
+                                  : tc_unit_cost(p, s, i % p.blocks_per_seq);
     if (i < kTcCachedPairs) cost[i] = c;
     atomicAdd(&red[0], c);
   }
@@ -1109,8 +1136,9 @@ struct TcUnit {
 };
 
 // Everything a role needs about list entry `e` (item id = (pair *
-// num_kv_heads + KV head) * kTcMaxParts + part, record base, ticket, parts);
-// n = 0 for a row block past the sequence's chunk.
+// num_kv_heads + KV head) * kTcMaxParts + part, record base, ticket | parts
+// << 24, the sequence's metadata), from shared memory only; n = 0 for a row
+// block past the sequence's chunk.
 __device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, const int* e) {
   TcUnit u;
   const int id = e[0];
@@ -1119,13 +1147,13 @@ __device__ __forceinline__ TcUnit tc_unit(const PrefillParams& p, const int* e) 
   const int pair = unit / p.num_kv_heads;
   u.kvh = unit - pair * p.num_kv_heads;
   u.rec = e[1];
-  u.ticket = e[2];
-  u.parts = e[3];
+  u.ticket = e[2] & 0xffffff;
+  u.parts = e[2] >> 24;
   u.s = pair / p.blocks_per_seq;
   const int rb = pair - u.s * p.blocks_per_seq;
-  u.q_start = __ldg(p.query_start_loc + u.s);
-  u.q_len = __ldg(p.query_start_loc + u.s + 1) - u.q_start;
-  u.seq_len = __ldg(p.seq_lens + u.s);
+  u.q_start = e[3];
+  u.q_len = e[4];
+  u.seq_len = e[5];
   u.ctx = u.seq_len - u.q_len;
   const int tpc = (kTcTiles * kTcRows) / p.group;
   u.tok_begin = rb * tpc;
@@ -1196,7 +1224,11 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
   int n_units = 0;
   while (n_units < kTcMaxUnitsPerCta && tc_snake_pos(n_units, blockIdx.x, gridDim.x) < total)
     ++n_units;
-  for (int k = warp; k < n_units; k += blockDim.x / 32) {
+  const int n_warps = blockDim.x / 32;
+  const int* seqc = scratch + kTcHistInts + 4 + kTcCachedPairs;
+  // the producer decodes unit 0, so it can fetch that unit's first page ids
+  // while the barriers and tensor memory are set up
+  for (int k = (warp + n_warps - kTcProducerWarp) % n_warps; k < n_units; k += n_warps) {
     const int pos = tc_snake_pos(k, blockIdx.x, gridDim.x);
     const int kvh = pos % p.num_kv_heads;
     int pair, part;
@@ -1208,9 +1240,31 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
     if (lane == 0) {
       int* e = units + k * kTcUnitInts;
       e[0] = (pair * p.num_kv_heads + kvh) * kTcMaxParts + part;
-      e[1] = parts_before * p.num_kv_heads + kvh * parts;  // first record of the unit
-      e[2] = n_before * p.num_kv_heads + kvh;              // its ticket
-      e[3] = parts;
+      e[1] = parts_before * p.num_kv_heads + kvh * parts;           // first record of the unit
+      e[2] = (n_before * p.num_kv_heads + kvh) | (parts << 24);     // its ticket, parts
+      const int s = pair / p.blocks_per_seq;
+      if (s < kTcSeqCache) {
+        e[3] = seqc[3 * s];
+        e[4] = seqc[3 * s + 1];
+        e[5] = seqc[3 * s + 2];
+      } else {
+        e[3] = __ldg(p.query_start_loc + s);
+        e[4] = __ldg(p.query_start_loc + s + 1) - e[3];
+        e[5] = __ldg(p.seq_lens + s);
+      }
+    }
+  }
+  // producer: unit 0 and the page ids of its first two tile groups (the loads
+  // stay in flight across the set-up below)
+  __syncwarp();
+  TcUnit pu{};
+  TilePages ppages{};
+  if (warp == kTcProducerWarp && n_units > 0) {
+    pu = tc_unit(p, units);
+    if (pu.n > 0) {
+      ppages = TilePages{p.block_tables + (int64_t)pu.s * p.block_table_stride,
+                         (pu.seq_len - 1) / p.block_size, p.block_size, lane, 0, 0, pu.lo >> 2};
+      ppages.init();
     }
   }
 
@@ -1254,16 +1308,30 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
     // ------------------------------------------------------------ producer --
     // Per unit: its Q (once the previous unit's S MMAs retired), then K0, K1,
     // (V_j, K_{j+2}) ... as in the one-unit kernel; stages and phases count
-    // the K and V tiles of all units in order.
+    // the K and V tiles of all units in order. The next unit's first page ids
+    // are read when a unit starts, a whole unit ahead of their use.
     int issued_k = 0, issued_v = 0, units_q = 0;
     int gk = 0, gv = 0;  // first global K / V tile index of the current unit
+    TcUnit U = pu;
+    TilePages pages = ppages;
     for (int k = 0; k < n_units && ok; ++k) {
-      const TcUnit U = tc_unit(p, units + k * kTcUnitInts);
-      if (U.n == 0) continue;
+      TcUnit un{};
+      TilePages next_pages{};
+      if (k + 1 < n_units) {
+        un = tc_unit(p, units + (k + 1) * kTcUnitInts);
+        if (un.n > 0) {
+          next_pages = TilePages{p.block_tables + (int64_t)un.s * p.block_table_stride,
+                                 (un.seq_len - 1) / p.block_size, p.block_size, lane, 0, 0,
+                                 un.lo >> 2};
+          next_pages.init();
+        }
+      }
+      if (U.n == 0) {
+        U = un;
+        pages = next_pages;
+        continue;
+      }
       const int max_page_idx = (U.seq_len - 1) / p.block_size;
-      TilePages pages{p.block_tables + (int64_t)U.s * p.block_table_stride, max_page_idx,
-                      p.block_size, lane, 0, 0, U.lo >> 2};
-      pages.init();
       // jj: tile of this part (0 .. n - 1); the unit's tile is U.lo + jj
       auto load = [&](bool is_v, int jj) -> bool {
         const int g = (is_v ? gv : gk) + jj;
@@ -1324,6 +1392,8 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
       }
       gk += n;
       gv += n;
+      U = un;
+      pages = next_pages;
     }
     if (!ok) {
       if (lane == 0) report_status(p.status, B200_STATUS_WAIT_TIMEOUT);
@@ -1814,8 +1884,13 @@ __global__ void __launch_bounds__(tc_threads<false>(), 1)
         uint4* orow = reinterpret_cast<uint4*>(
             reinterpret_cast<T*>(p.out) + (int64_t)(U.q_start + row_token) * p.out_token_stride +
             (int64_t)row_head * p.out_head_stride);
+        if (p.out_v8) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) orow[i] = packed[i];
+          for (int i = 0; i < 8; ++i) st_global_v8(orow + 2 * i, packed[2 * i], packed[2 * i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) orow[i] = packed[i];
+        }
       }
       ++ep;
       gv += U.n;
