@@ -329,7 +329,9 @@ B200_API int b200_paged_decode_noalloc(const void* q, int64_t q_seq_stride,
  * of device memory, 256-byte aligned. With it, 16-bit caches whose GQA group
  * divides 128 split the KV range of units much longer than the batch's
  * average work per SM over several CTAs (partial results merged in the
- * workspace): a long chunk on a long cached prefix then uses the whole GPU.
+ * workspace), when the launch has at most half as many (sequence, row
+ * block, KV head) units as SMs or more than two per SM: a short chunk on a
+ * long cached prefix then uses the whole GPU.
  * Zero the workspace once before its first use; a launch leaves its
  * counters zero again, unless it reports an error in *status, after which
  * the workspace must be zeroed again. Launches that share one workspace

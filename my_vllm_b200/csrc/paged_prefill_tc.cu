@@ -975,7 +975,7 @@ __device__ __forceinline__ int tc_cached_cost(const PrefillParams& p, const int*
 // tc_build_hist (its 4 result ints serve as reduction slots).
 __device__ __forceinline__ int tc_build_split_hist(const PrefillParams& p, int* scratch) {
   int* hist = scratch;
-  int* red = scratch + kTcHistInts;  // [0] total tiles, [1] split parts, [2] target
+  int* red = scratch + kTcHistInts;  // [0] total tiles, [1] split parts, [2] split pairs, [3] items
   int* cost = scratch + kTcHistInts + 4;
   int* seqc = cost + kTcCachedPairs;  // [kTcSeqCache][3]
   const int pairs = p.num_seqs * p.blocks_per_seq;
@@ -1004,20 +1004,33 @@ __device__ __forceinline__ int tc_build_split_hist(const PrefillParams& p, int* 
   if (p.split_cap > 0 && p.num_sms > 0) {
     const int64_t total = (int64_t)red[0] * p.num_kv_heads;
     const int64_t avg = (total + p.num_sms - 1) / p.num_sms;
+    const bool one_wave = (int64_t)pairs * p.num_kv_heads <= p.num_sms;
     target = avg > kTcMinPartTiles ? (int)avg : kTcMinPartTiles;
     for (int round = 0; round < 64; ++round) {
       __syncthreads();
-      if (threadIdx.x == 0) red[1] = 0;
+      if (threadIdx.x == 0) {
+        red[1] = 0;
+        red[2] = 0;
+      }
       __syncthreads();
       for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
         const int parts = tc_parts(tc_cached_cost(p, cost, i), target);
-        if (parts > 1) atomicAdd(&red[1], parts);
+        if (parts > 1) {
+          atomicAdd(&red[1], parts);
+          atomicAdd(&red[2], 1);  // split pairs
+        }
       }
       __syncthreads();
-      if ((int64_t)red[1] * p.num_kv_heads <= p.split_cap) break;
+      // the parts fit the records, and when every unit has its own SM the
+      // items still do (a part in a second wave costs more than it saves)
+      const int64_t items = (int64_t)(pairs + red[1] - red[2]) * p.num_kv_heads;
+      if ((int64_t)red[1] * p.num_kv_heads <= p.split_cap && (!one_wave || items <= p.num_sms))
+        break;
       target += target / 4 + 1;
     }
-    if ((int64_t)red[1] * p.num_kv_heads > p.split_cap) target = 0;  // never split then
+    const int64_t items = (int64_t)(pairs + red[1] - red[2]) * p.num_kv_heads;
+    if ((int64_t)red[1] * p.num_kv_heads > p.split_cap || (one_wave && items > p.num_sms))
+      target = 0;  // never split then
   }
   for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
     const int c = tc_cached_cost(p, cost, i);
@@ -1925,15 +1938,26 @@ static cudaError_t launch_tc_typed(const CUtensorMap& mk, const CUtensorMap& mv,
   const int64_t units = (int64_t)blocks * num_kv_heads * num_seqs;
   if (units > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if constexpr (!kFp8) {
+    int dev = 0, sms = 0;
     if (q.q_tma) {
+      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    }
+    // The persistent kernel where it pays: more than two units per SM (its per-CTA
+    // set-up is paid once, not per unit), or at most half an SM wave of units with
+    // a split-KV workspace (a few long units cut into parts on the idle SMs: one
+    // 64-token chunk on an 8k prefix, 158 -> 50 us). Otherwise the one-unit kernel
+    // is faster: the hardware hands second-wave units to the SMs that finish first,
+    // whole output tiles leave by TMA store, and nothing is set up per list (L2
+    // cold: 128 units 56 vs 64 us, config 3's 256 units 68.6 vs 72.7 us).
+    const bool persistent = q.q_tma && sms > 0 &&
+                            (units > 2 * (int64_t)sms || (q.split_cap > 0 && 2 * units <= sms));
+    if (persistent) {
       // persistent: one CTA per SM (at most kTcMaxUnitsPerCta units each)
       auto pkernel = paged_prefill_tc_persistent_kernel<T>;
       e = ensure_smem_attr(reinterpret_cast<const void*>(pkernel), kTcPersistSmem);
       if (e != cudaSuccess) return e;
-      int dev = 0, sms = 0;
-      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return e;
       q.num_sms = sms;
       // split parts add at most split_cap items to the units
       const int64_t items = units + (q.split_cap > 0 ? q.split_cap : 0);

@@ -427,3 +427,22 @@ def test_prefill_split_kv_matches_oracle(cuda_device, case):
         assert_close_to_oracle(out, expected, w.q.dtype)
     assert (outs[1].float() - outs[0].float()).abs().max().item() <= MAX_ABS[w.q.dtype]
     assert torch.equal(outs[1].view(torch.int16), outs[2].view(torch.int16))
+
+
+@pytest.mark.parametrize("with_workspace", [False, True])
+def test_prefill_many_units_per_sm(cuda_device, with_workspace):
+    """More than two (sequence, row block, KV head) units per SM: the launch
+    takes the persistent kernel (one CTA per SM walking a unit list, unit
+    metadata from its shared-memory list, the next unit's page ids read a unit
+    ahead). 4 chunks of 640 tokens on prefixes of 0/256/640/1024 tokens, GQA 4:
+    320 units on 148 SMs. Every row matches the oracle."""
+    w = workloads.config3(device=cuda_device, num_decode=0, chunk=640, hits=(0, 256, 640, 1024))
+    ws = (torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=cuda_device)
+          if with_workspace else None)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    out = torch.full_like(w.q, float("nan"))
+    ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, w.query_start_loc,
+                      out, 640, 128 ** -0.5, status=status, workspace=ws)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
