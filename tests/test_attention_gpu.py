@@ -407,8 +407,8 @@ def test_prefill_split_kv_matches_oracle(cuda_device, case):
         w = workloads.config3(device=cuda_device, num_decode=0, hits=(16384,), chunk=64)
     elif case == "config3":
         w = workloads.config3(device=cuda_device, num_decode=0)
-    else:
-        w = workloads.small_case([40, 200], [9000, 3200], 2, Hq=64, Hkv=8, device=cuda_device)
+    else:  # GQA 8, 64 units (at most half an SM wave, so the split path runs)
+        w = workloads.small_case([40, 100], [9000, 3200], 2, Hq=64, Hkv=8, device=cuda_device)
     qsl = w.extra["qsl_host"]
     max_q = max(qsl[i + 1] - qsl[i] for i in range(w.num_seqs))
     ws = torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=cuda_device)
@@ -430,13 +430,17 @@ def test_prefill_split_kv_matches_oracle(cuda_device, case):
 
 
 @pytest.mark.parametrize("with_workspace", [False, True])
-def test_prefill_many_units_per_sm(cuda_device, with_workspace):
+@pytest.mark.parametrize("hq", [32, 64])
+def test_prefill_many_units_per_sm(cuda_device, with_workspace, hq):
     """More than two (sequence, row block, KV head) units per SM: the launch
     takes the persistent kernel (one CTA per SM walking a unit list, unit
     metadata from its shared-memory list, the next unit's page ids read a unit
-    ahead). 4 chunks of 640 tokens on prefixes of 0/256/640/1024 tokens, GQA 4:
-    320 units on 148 SMs. Every row matches the oracle."""
+    ahead). 4 chunks of 640 tokens on prefixes of 0/256/640/1024 tokens, 8 KV
+    heads, GQA 4 or 8: 320 or 640 units on 148 SMs. Every row matches the oracle."""
     w = workloads.config3(device=cuda_device, num_decode=0, chunk=640, hits=(0, 256, 640, 1024))
+    if hq != w.num_q_heads:
+        w = workloads.small_case([640] * 4, w.extra["seq_lens_host"], 4, Hq=hq, Hkv=8,
+                                 device=cuda_device)
     ws = (torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=cuda_device)
           if with_workspace else None)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
