@@ -450,3 +450,24 @@ def test_prefill_many_units_per_sm(cuda_device, with_workspace, hq):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
+
+
+@pytest.mark.parametrize("with_workspace", [False, True])
+def test_prefill_many_units_ragged_chunks(cuda_device, with_workspace):
+    """The persistent kernel with ragged chunks: units are counted from the
+    longest chunk, so most (sequence, row block) units of the short chunks are
+    empty and every CTA's list mixes real and empty ones. 6 chunks of
+    640/17/300/1/513/64 tokens on KV lengths up to 2,600, GQA 4: 480 units,
+    more than two per SM. Every row matches the oracle (the output starts as NaN)."""
+    q_lens = [640, 17, 300, 1, 513, 64]
+    kv_lens = [1700, 2600, 300, 900, 513, 2000]
+    w = workloads.small_case(q_lens, kv_lens, len(q_lens), Hq=32, Hkv=8, device=cuda_device)
+    ws = (torch.zeros(ops.prefill_workspace_bytes(), dtype=torch.uint8, device=cuda_device)
+          if with_workspace else None)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    out = torch.full_like(w.q, float("nan"))
+    ops.paged_prefill(w.q, w.k_cache, w.v_cache, w.block_tables, w.seq_lens, w.query_start_loc,
+                      out, max(q_lens), 128 ** -0.5, status=status, workspace=ws)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert_close_to_oracle(out, oracle_all_rows(w), w.q.dtype)
